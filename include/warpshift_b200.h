@@ -1,0 +1,149 @@
+/*
+ * warpshift_b200 C ABI: in-place BF16 model switching driven by an
+ * entropy-coded delta stream, decoded and applied on B200 (sm_100a).
+ *
+ * The reference (DrRyanHuang/WarpShift) is pure Python. Its delta path is the
+ * class warpshift/delta.py:95-327 DeltaWeights, whose prepare step encodes with
+ * nvCOMP ANS and whose apply step runs nvCOMP's batched ANS decode followed by
+ * the Triton kernel _restore_batch. These entry points replace that machinery;
+ * warpshift_b200/delta.py binds them with ctypes behind the same Python API.
+ *
+ * Conventions: every function returns WS_OK (0) or a WS_ERR_* status, never
+ * throws across the ABI, and records a message readable with ws_last_error()
+ * on the calling thread. Streams are cudaStream_t passed as void*. No torch
+ * types appear here; tensors are raw pointers plus byte counts.
+ */
+#ifndef WARPSHIFT_B200_H
+#define WARPSHIFT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define WS_API __attribute__((visibility("default")))
+#else
+#define WS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WS_OK 0
+#define WS_ERR_INVALID 1  /* bad argument / layout (maps to ValueError, as delta.py:139-162) */
+#define WS_ERR_CUDA 2     /* CUDA runtime failure */
+#define WS_ERR_DEVICE 3   /* device-side decode error: corrupt frame, state or length mismatch */
+#define WS_ERR_CHECKSUM 4 /* written bytes do not hash to the value recorded at prepare */
+#define WS_ERR_NOMEM 5    /* host or device allocation failed */
+#define WS_ERR_STATE 6    /* call out of order (e.g. apply before upload) */
+
+#define WS_POLICY_AUTO 0 /* delta.py:176-194: raw XOR, else grouped/odd XOR-ANS, else U16-ANS if strictly smaller */
+#define WS_POLICY_XOR 1  /* only XOR representations (modes 0/1/2) */
+#define WS_POLICY_U16 2  /* BF16 packets try only U16-ANS (raw XOR if not smaller); others follow AUTO */
+
+typedef struct ws_plan ws_plan;
+
+/* One tensor of the A/B pair, in delta.py:147-158 order (gpu_target dict order). */
+typedef struct ws_tensor_desc {
+  const void* base;   /* host address of A's bytes (cpu_base tensor) */
+  const void* target; /* B's bytes: device address on opts->device if target_on_device, else host */
+  uint64_t nbytes;    /* tensor byte size (numel * element_size); may be 0 */
+  int32_t is_bf16;    /* BF16 tensors may use the U16 mode (delta.py:190) */
+  int32_t reserved;
+} ws_tensor_desc;
+
+typedef struct ws_build_options {
+  int32_t policy;           /* WS_POLICY_* */
+  int32_t threads;          /* host encoder threads; 0 = all online CPUs */
+  int32_t target_on_device; /* 1: target pointers are device addresses (normal prepare) */
+  int32_t device;           /* CUDA device ordinal of the targets */
+  uint64_t batch_bytes;     /* bound on one H2D staging batch (0 = 16 MiB) */
+  int32_t staging_slots;    /* device staging buffers (0 = 3) */
+  int32_t pin_arena;        /* 1: arena in pinned host memory (needs CUDA); 0: malloc */
+} ws_build_options;
+
+typedef struct ws_plan_stats {
+  uint64_t runtime_bytes;      /* sum of tensor bytes (delta.py:122) */
+  uint64_t skipped_bytes;      /* bytes of all-zero 16 MiB packets (delta.py:211) */
+  uint64_t zero_block_bytes;   /* bytes of all-zero 64 KiB blocks inside written packets */
+  uint64_t touched_bytes;      /* weight bytes the kernel reads and writes per apply */
+  uint64_t payload_bytes;      /* sum of packet payload sizes (delta.py:124) */
+  uint64_t arena_bytes;        /* bytes staged host->device per apply (delta.py:125) */
+  uint64_t table_bytes;        /* device decode tables */
+  uint64_t metadata_bytes;     /* device block/tile descriptors + tables */
+  uint64_t scratch_bytes;      /* device staging slots (+ resident copy when enabled) */
+  uint64_t mode_counts[5];     /* packets per ws mode: XOR_RAW, XOR_GROUP2_ANS, XOR_ANS, U16_ANS, SKIP */
+  uint64_t blocks, tiles, batches, packets;
+  uint64_t expected_checksum[2]; /* [0] after forward (A->B), [1] after reverse (B->A) */
+  double encode_seconds;
+} ws_plan_stats;
+
+typedef struct ws_apply_result {
+  uint64_t checksum;         /* checksum of the bytes written by this apply */
+  uint64_t expected;         /* checksum recorded at prepare for this direction */
+  uint32_t device_errors;    /* OR of device error bits (see ws_format.h WS_DEVERR_*) */
+  uint32_t bad_block_plus1;  /* 1 + index of a failing block, 0 if none */
+  uint64_t h2d_bytes;        /* bytes copied host->device by this apply */
+  uint32_t launches;         /* decode kernel launches issued */
+  uint32_t reserved;
+} ws_apply_result;
+
+/* Host-side view of a built plan, for checkers and CPU baselines. */
+typedef struct ws_plan_view {
+  const void* blocks;     /* ws_block_desc[nblocks] (ws_format.h) */
+  uint64_t nblocks;
+  const void* tiles;      /* ws_tile_desc[ntiles] */
+  uint64_t ntiles;
+  const uint32_t* tables; /* 512 slot entries per packet table */
+  uint64_t ntables;
+  const uint8_t* arena;   /* host arena holding every block payload */
+  uint64_t arena_bytes;
+} ws_plan_view;
+
+/* Library version (major*10000 + minor*100 + patch). */
+WS_API int ws_version(void);
+
+/* Copies the calling thread's last error message (NUL-terminated, truncated). */
+WS_API int ws_last_error(char* buf, size_t len);
+
+/* Replaces delta.py:26-34 _u16_residual: out = low-byte plane || high-byte plane of
+ * zigzag((B - A) mod 2^16); nbytes must be even. Host only. */
+WS_API int ws_u16_residual(const uint8_t* base, const uint8_t* target, uint64_t nbytes, uint8_t* out);
+
+/* Replaces the prepare half of DeltaWeights.__init__ (delta.py:102-135: _bind_tensors'
+ * overlap check 137-162, _encode_packets 196-216, _encode_chunk 176-194, _compress
+ * 164-174, _prepare_batches/_pack_batch 218-280). Copies B device->host in 16 MiB
+ * packets on `stream`, encodes every packet on `threads` host threads, lays out the
+ * arena and descriptors. Allocates no device memory. */
+WS_API int ws_plan_build(const ws_tensor_desc* tensors, uint64_t ntensors, const ws_build_options* opts,
+                  void* stream, ws_plan** out);
+
+/* Allocates device metadata and staging slots and uploads descriptors/tables
+ * (the device half of delta.py:218-280). */
+WS_API int ws_plan_upload(ws_plan* plan, void* stream);
+
+/* resident=1 keeps a device copy of the whole arena so applies skip the H2D
+ * staging (kernel-only timing); resident=0 frees it. */
+WS_API int ws_plan_set_resident(ws_plan* plan, int resident, void* stream);
+
+/* Replaces DeltaWeights.apply (delta.py:294-327): A->B when reverse == 0, B->A when 1.
+ * Stages the arena H2D on copy_stream in bounded batches, decodes and applies each
+ * batch on compute_stream, reads back the device result, and returns after
+ * compute_stream completes. Returns WS_ERR_DEVICE or WS_ERR_CHECKSUM on failure. */
+WS_API int ws_apply(ws_plan* plan, int reverse, void* compute_stream, void* copy_stream, ws_apply_result* out);
+
+/* Asynchronous halves of ws_apply: enqueue only (no host synchronisation), then
+ * wait for compute_stream and evaluate the result. */
+WS_API int ws_apply_async(ws_plan* plan, int reverse, void* compute_stream, void* copy_stream);
+WS_API int ws_apply_finish(ws_plan* plan, void* compute_stream, ws_apply_result* out);
+
+WS_API int ws_plan_get_stats(const ws_plan* plan, ws_plan_stats* out);
+WS_API int ws_plan_get_view(const ws_plan* plan, ws_plan_view* out);
+
+/* Frees host and device resources (delta.py relies on GC for the same). */
+WS_API void ws_plan_destroy(ws_plan* plan);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WARPSHIFT_B200_H */

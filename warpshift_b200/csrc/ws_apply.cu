@@ -1,0 +1,384 @@
+// Fused rANS decode + in-place XOR / wrapping-u16 apply for B200 (sm_100a).
+//
+// Replaces, in one kernel, nvCOMP's batched ANS decode into a scratch buffer
+// (warpshift/delta.py:313-316) and the Triton read-modify-write kernel
+// _restore_batch (delta.py:60-92, launched at 317-324). The decoded residual
+// never touches HBM: per 64 KiB block the kernel reads the compressed payload
+// once and reads + writes the destination weights once.
+//
+// Work decomposition: one CTA (16 warps) per tile of up to 16 blocks of one
+// packet; one warp per block. The packet's two 256-slot decode tables are
+// replicated 32 times in shared memory so that lane l always reads bank l
+// (conflict-free random lookups). Each warp streams its compressed payload
+// from HBM into a 2 x 1 KiB shared-memory ring with cp.async.bulk (TMA bulk
+// copies, no multicast) completing on per-slot mbarriers.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ws_format.h"
+#include "ws_kernels.h"
+
+namespace ws {
+
+namespace {
+
+constexpr uint32_t kWarps = WS_TILE_BLOCKS;
+constexpr uint32_t kThreads = kWarps * 32;
+constexpr uint32_t kTableWords = 256 * 32;                  // one replicated plane table
+constexpr uint32_t kRingOffset = 2 * kTableWords * 4;       // bytes
+constexpr uint32_t kBarOffset = kRingOffset + kWarps * WS_RING_BYTES;
+constexpr uint32_t kSmemBytes = kBarOffset + kWarps * 2 * 8;
+constexpr uint32_t kRingHalfwords = WS_RING_BYTES / 2;      // 1024
+constexpr uint32_t kHalfHalfwords = WS_RING_HALF_BYTES / 2; // 512
+constexpr uint32_t kWaitLimit = 1u << 22;                   // bounded spin on a staging barrier
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint32_t lanemask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+// PRMT in its default mode: a selector nibble with bit 3 set replicates the
+// sign bit of the selected byte.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// Returns true when the phase with the given parity has completed, false if
+// the bounded wait gave up.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  for (uint32_t it = 0; it < kWaitLimit; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void report(ws_device_result* res, uint32_t err, uint32_t block) {
+  atomicOr(&res->errors, err);
+  atomicExch(&res->bad_block_plus1, block + 1);
+}
+
+// d = unzigzag in rotated form: y ^ (sign ? 0x7FFF : 0) per 16-bit half.
+// Returns d & 0x7FFF7FFF in *dm; bit 15 of each half of d equals that of y.
+__device__ __forceinline__ uint32_t u16_apply(uint32_t old, uint32_t y, bool reverse) {
+  const uint32_t sign = prmt(y, 0, 0xBB99);          // 0xFFFF per half with bit 15 set
+  const uint32_t dm = (y ^ sign) & 0x7FFF7FFFu;      // low 15 bits of d
+  if (!reverse) {
+    const uint32_t s = (old & 0x7FFF7FFFu) + dm;
+    return s ^ ((old ^ y) & 0x80008000u);
+  } else {
+    const uint32_t s = (old | 0x80008000u) - dm;
+    return s ^ ((old ^ y ^ 0x80008000u) & 0x80008000u);
+  }
+}
+
+struct Checksum {
+  uint32_t a = 0, b = 0;
+  __device__ __forceinline__ void add(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
+    a += w0 + w1 + w2 + w3;
+    b += a;
+  }
+  __device__ __forceinline__ void finish(uint32_t lane, uint32_t block, ws_device_result* res) const {
+    unsigned long long h = ws_lane_hash(a, b, lane);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) h += __shfl_xor_sync(0xFFFFFFFFu, h, o);
+    if (lane == 0) atomicAdd(&res->checksum, (unsigned long long)ws_block_hash(h, block));
+  }
+};
+
+// Slow path for one lane's 16-byte chunk of a group: partial group, odd tail,
+// or a destination that is not 16-byte aligned. r[0..3] hold the lane's 8
+// residual words (XOR value or rotated zigzag word); bytes below coded_bytes
+// are coded words, a byte at coded_bytes is the block's uncoded odd tail.
+// Fully unrolled so that r[] and out[] stay in registers.
+template <bool U16, bool REVERSE>
+__device__ __forceinline__ void apply_chunk_bytes(uint8_t* p, uint32_t first_byte, uint32_t nbytes,
+                                                  const uint32_t (&r)[4], uint32_t coded_bytes, uint8_t tail,
+                                                  uint32_t (&out)[4]) {
+#pragma unroll
+  for (uint32_t j = 0; j < 8; ++j) {
+    const uint32_t bi = first_byte + 2 * j;
+    const uint32_t rw = (r[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;
+    uint32_t nw = 0;
+    if (bi < coded_bytes) {  // coded words come in byte pairs
+      const uint32_t old = (uint32_t)p[2 * j] | ((uint32_t)p[2 * j + 1] << 8);
+      if (U16)
+        nw = u16_apply(old, rw, REVERSE) & 0xFFFFu;
+      else
+        nw = old ^ rw;
+      p[2 * j] = (uint8_t)(nw & 0xFF);
+      p[2 * j + 1] = (uint8_t)(nw >> 8);
+    } else if (bi < nbytes) {  // the uncoded odd last byte of the block
+      nw = (uint32_t)(uint8_t)(p[2 * j] ^ tail);
+      p[2 * j] = (uint8_t)nw;
+    }
+    out[j >> 1] |= nw << (16 * (j & 1));
+  }
+}
+
+__device__ void raw_block(const ws_block_desc& bd, uint32_t block, const uint8_t* __restrict__ src, uint32_t lane,
+                          ws_device_result* res) {
+  uint8_t* dst = reinterpret_cast<uint8_t*>(bd.dst);
+  const uint32_t n = bd.nbytes;
+  const uint32_t groups = (n + WS_GROUP_BYTES - 1) / WS_GROUP_BYTES;
+  const bool aligned = (bd.dst & 15u) == 0;
+  Checksum ck;
+#pragma unroll 1
+  for (uint32_t g = 0; g < groups; ++g) {
+    const uint32_t off = g * WS_GROUP_BYTES + lane * 16u;
+    if (aligned && (g + 1) * WS_GROUP_BYTES <= n) {
+      const uint4 r = __ldg(reinterpret_cast<const uint4*>(src + off));
+      uint4* d = reinterpret_cast<uint4*>(dst + off);
+      uint4 v = *d;
+      v.x ^= r.x;
+      v.y ^= r.y;
+      v.z ^= r.z;
+      v.w ^= r.w;
+      *d = v;
+      ck.add(v.x, v.y, v.z, v.w);
+    } else {
+      uint32_t out[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (uint32_t k = 0; k < 16; ++k) {
+        if (off + k < n) {
+          const uint8_t nv = (uint8_t)(dst[off + k] ^ src[off + k]);
+          dst[off + k] = nv;
+          out[k >> 2] |= (uint32_t)nv << (8 * (k & 3));
+        }
+      }
+      ck.add(out[0], out[1], out[2], out[3]);
+    }
+  }
+  ck.finish(lane, block, res);
+}
+
+// Decode one step for both planes: word = sym0 | sym1 << 8.
+#define WS_DECODE_STEP(ea, eb)                                   \
+  {                                                              \
+    ea = tbl0[((xa & 255u) << 5) | lane];                        \
+    eb = tbl1[((xb & 255u) << 5) | lane];                        \
+    xa = (ea >> 16) * (xa >> 8) + (ea & 255u);                   \
+    xb = (eb >> 16) * (xb >> 8) + (eb & 255u);                   \
+  }
+
+// Renormalisation check: plane-0 reads first in lane order, then plane 1.
+#define WS_RENORM()                                                                   \
+  {                                                                                   \
+    const bool na = xa < WS_RANS_L, nb = xb < WS_RANS_L;                              \
+    const uint32_t ba = __ballot_sync(0xFFFFFFFFu, na);                               \
+    const uint32_t bb = __ballot_sync(0xFFFFFFFFu, nb);                               \
+    const uint32_t ca = __popc(ba);                                                   \
+    if (na) xa = (xa << 16) | ring16[(pos + __popc(ba & ltm)) & (kRingHalfwords - 1)]; \
+    if (nb) xb = (xb << 16) | ring16[(pos + ca + __popc(bb & ltm)) & (kRingHalfwords - 1)]; \
+    pos += ca + __popc(bb);                                                           \
+  }
+
+template <bool U16, bool REVERSE>
+__device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t* __restrict__ src,
+                          const uint32_t* __restrict__ tbl0, const uint32_t* __restrict__ tbl1, uint8_t* ring,
+                          uint32_t bar_base, uint32_t lane, ws_device_result* res) {
+  uint8_t* dst = reinterpret_cast<uint8_t*>(bd.dst);
+  const uint32_t n = bd.nbytes;
+  const uint32_t W = n / 2;
+  const uint32_t coded_bytes = 2 * W;
+  const uint32_t dec_groups = (W + WS_GROUP_WORDS - 1) / WS_GROUP_WORDS;
+  const uint32_t groups = (n + WS_GROUP_BYTES - 1) / WS_GROUP_BYTES;
+  const bool aligned = (bd.dst & 15u) == 0;
+  const uint32_t total_halves = (bd.clen + WS_RING_HALF_BYTES - 1) / WS_RING_HALF_BYTES;
+  const uint32_t ring_s = smem_addr(ring);
+  const uint16_t* ring16 = reinterpret_cast<const uint16_t*>(ring);
+  const uint32_t ltm = lanemask_lt();
+
+  auto issue = [&](uint32_t k) {
+    if (lane == 0 && k < total_halves) {
+      const uint32_t off = k * WS_RING_HALF_BYTES;
+      const uint32_t bytes = min(WS_RING_HALF_BYTES, bd.clen - off);
+      bulk_load(ring_s + (k & 1u) * WS_RING_HALF_BYTES, src + off, bytes, bar_base + (k & 1u) * 8u);
+    }
+  };
+  uint32_t issued = min(2u, total_halves);
+  issue(0);
+  issue(1);
+  uint32_t ready = 0;
+  bool ok = true;
+  if (total_halves > 0) {
+    ok = mbar_wait(bar_base, 0);
+    ready = 1;
+  }
+  uint32_t xa = reinterpret_cast<const uint32_t*>(ring)[lane];
+  uint32_t xb = reinterpret_cast<const uint32_t*>(ring)[32 + lane];
+  uint32_t pos = WS_HEADER_HALFWORDS;
+  Checksum ck;
+
+#pragma unroll 1
+  for (uint32_t g = 0; g < groups && ok; ++g) {
+    const uint32_t off = g * WS_GROUP_BYTES + lane * 16u;
+    const bool vec = aligned && (g + 1) * WS_GROUP_BYTES <= coded_bytes;
+    uint4 old = make_uint4(0, 0, 0, 0);
+    if (vec) old = *reinterpret_cast<const uint4*>(dst + off);
+    uint32_t r[4] = {0, 0, 0, 0};
+    if (g < dec_groups) {
+      // Recycle the slot whose half has been consumed, then make sure every
+      // halfword this group can read ([pos, pos + 256)) has landed.
+      while (issued < total_halves && pos >= kHalfHalfwords * (issued - 1)) {
+        __syncwarp();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        issue(issued);
+        ++issued;
+      }
+      const uint32_t need = min(pos + 256u, bd.nwords);
+      while (ready < issued && need > kHalfHalfwords * ready) {
+        ok = mbar_wait(bar_base + (ready & 1u) * 8u, (ready >> 1) & 1u);
+        if (!ok) break;
+        ++ready;
+      }
+      if (!ok) break;
+      uint32_t ea0, eb0, ea1, eb1;
+      if ((g + 1) * WS_GROUP_WORDS <= W) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          WS_DECODE_STEP(ea0, eb0);
+          WS_DECODE_STEP(ea1, eb1);
+          r[c] = __byte_perm(__byte_perm(ea0, eb0, 0x0051), __byte_perm(ea1, eb1, 0x5100), 0x7610);
+          WS_RENORM();
+        }
+      } else {
+        const int first = (int)(g * WS_GROUP_WORDS + lane * WS_WORDS_PER_LANE);
+        const int valid = max(0, min(8, (int)W - first));
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          ea0 = eb0 = ea1 = eb1 = 0;
+          if (2 * c < valid) WS_DECODE_STEP(ea0, eb0);
+          if (2 * c + 1 < valid) WS_DECODE_STEP(ea1, eb1);
+          r[c] = __byte_perm(__byte_perm(ea0, eb0, 0x0051), __byte_perm(ea1, eb1, 0x5100), 0x7610);
+          WS_RENORM();
+        }
+      }
+    }
+    if (vec) {
+      uint4 v;
+      if (U16) {
+        v.x = u16_apply(old.x, r[0], REVERSE);
+        v.y = u16_apply(old.y, r[1], REVERSE);
+        v.z = u16_apply(old.z, r[2], REVERSE);
+        v.w = u16_apply(old.w, r[3], REVERSE);
+      } else {
+        v.x = old.x ^ r[0];
+        v.y = old.y ^ r[1];
+        v.z = old.z ^ r[2];
+        v.w = old.w ^ r[3];
+      }
+      *reinterpret_cast<uint4*>(dst + off) = v;
+      ck.add(v.x, v.y, v.z, v.w);
+    } else {
+      uint32_t out[4] = {0, 0, 0, 0};
+      apply_chunk_bytes<U16, REVERSE>(dst + off, off, n, r, coded_bytes, bd.tail, out);
+      ck.add(out[0], out[1], out[2], out[3]);
+    }
+  }
+  if (!ok) {
+    if (lane == 0) report(res, WS_DEVERR_TIMEOUT, block);
+  } else {
+    const bool states_ok = __all_sync(0xFFFFFFFFu, xa == WS_RANS_L && xb == WS_RANS_L);
+    if (lane == 0) {
+      if (!states_ok) report(res, WS_DEVERR_STATE, block);
+      if (pos != bd.nwords) report(res, WS_DEVERR_LENGTH, block);
+    }
+  }
+  // Never leave a bulk copy in flight into shared memory of an exiting CTA.
+  while (ready < issued) {
+    if (!mbar_wait(bar_base + (ready & 1u) * 8u, (ready >> 1) & 1u)) {
+      if (lane == 0) report(res, WS_DEVERR_TIMEOUT, block);
+      break;
+    }
+    ++ready;
+  }
+  ck.finish(lane, block, res);
+}
+
+template <bool REVERSE>
+__global__ void __launch_bounds__(kThreads, 2)
+    ws_apply_kernel(const ws_tile_desc* __restrict__ tiles, uint32_t tile_begin,
+                    const ws_block_desc* __restrict__ blocks, const uint32_t* __restrict__ tables,
+                    const uint8_t* __restrict__ payload, uint64_t payload_offset, ws_device_result* res) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint32_t* tbl = reinterpret_cast<uint32_t*>(smem);
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  const ws_tile_desc tile = tiles[tile_begin + blockIdx.x];
+  if (tile.table != WS_NO_TABLE) {
+    // Thread t expands slot entry t (plane t >> 8) into its 32 replicas; the
+    // rotated segment order keeps 8 consecutive threads on distinct banks.
+    const uint32_t t = threadIdx.x;
+    const uint32_t e = __ldg(tables + (uint64_t)tile.table * 512u + t);
+    const uint4 v = make_uint4(e, e, e, e);
+    uint4* row = reinterpret_cast<uint4*>(tbl + (t >> 8) * kTableWords + (t & 255u) * 32u);
+#pragma unroll
+    for (uint32_t k = 0; k < 8; ++k) row[(k + t) & 7u] = v;
+  }
+  const uint32_t bar_base = smem_addr(smem + kBarOffset) + warp * 16u;
+  if (lane == 0) {
+    mbar_init(bar_base, 1);
+    mbar_init(bar_base + 8, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (warp >= tile.nblocks) return;
+  const uint32_t block = tile.first_block + warp;
+  const ws_block_desc bd = blocks[block];
+  const uint8_t* src = payload + (bd.src - payload_offset);
+  uint8_t* ring = smem + kRingOffset + warp * WS_RING_BYTES;
+  switch (bd.kind) {
+    case WS_KIND_RAW:
+      raw_block(bd, block, src, lane, res);
+      break;
+    case WS_KIND_ANS_XOR:
+      ans_block<false, REVERSE>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
+      break;
+    case WS_KIND_ANS_U16:
+      ans_block<true, REVERSE>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
+      break;
+    default:
+      if (lane == 0) report(res, WS_DEVERR_KIND, block);
+  }
+}
+
+}  // namespace
+
+size_t apply_smem_bytes() { return kSmemBytes; }
+
+cudaError_t launch_apply(const ws_tile_desc* tiles, uint32_t tile_begin, uint32_t ntiles,
+                         const ws_block_desc* blocks, const uint32_t* tables, const uint8_t* payload,
+                         uint64_t payload_offset, ws_device_result* result, int reverse, cudaStream_t stream) {
+  if (ntiles == 0) return cudaSuccess;
+  auto kernel = reverse ? ws_apply_kernel<true> : ws_apply_kernel<false>;
+  // Set on every launch: the attribute is per device context and costs ~1 us.
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+  if (e != cudaSuccess) return e;
+  kernel<<<ntiles, kThreads, kSmemBytes, stream>>>(tiles, tile_begin, blocks, tables, payload, payload_offset,
+                                                     result);
+  return cudaGetLastError();
+}
+
+}  // namespace ws

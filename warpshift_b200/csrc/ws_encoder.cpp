@@ -1,0 +1,362 @@
+// Host encoder: chooses each packet's mode with the reference rule
+// (warpshift/delta.py:176-194) and codes ANS modes with this project's
+// interleaved rANS format (ws_format.h).
+#include "ws_encoder.h"
+
+#include <string.h>
+
+#include <cmath>
+
+namespace ws {
+
+namespace {
+
+inline uint32_t round_up16(uint32_t v) { return (v + (WS_PAYLOAD_ALIGN - 1)) & ~(WS_PAYLOAD_ALIGN - 1); }
+
+// U16 representation coded by this format: y = rotr16(zigzag(d), 1) with
+// d = (target - base) mod 2^16, so the sign sits in bit 15 and the magnitude in
+// bits 0..14. The reference's residual is zigzag(d) itself (delta.py:32-33);
+// both are bijections of d, so the applied result is the same.
+inline uint16_t u16_symbol_word(uint16_t b, uint16_t t) {
+  int32_t d = (int32_t)(int16_t)(uint16_t)(t - b);
+  uint32_t z = ((uint32_t)(d * 2) ^ (uint32_t)(d >> 15)) & 0xFFFFu;
+  return (uint16_t)((z >> 1) | ((z & 1u) << 15));
+}
+
+inline uint16_t load_u16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+struct PlaneTables {
+  uint32_t freq[2][256];
+  uint32_t cdf[2][256];
+};
+
+void tables_from_counts(const uint64_t counts[2][256], PlaneTables* t, uint32_t entries[512]) {
+  for (int p = 0; p < 2; ++p) {
+    quantize_frequencies(counts[p], t->freq[p]);
+    uint32_t c = 0;
+    for (int s = 0; s < 256; ++s) {
+      t->cdf[p][s] = c;
+      c += t->freq[p][s];
+    }
+    build_slot_entries(t->freq[p], entries + 256 * p);
+  }
+}
+
+// Encode the two planes of one block (W words) in the decoder's interleaved
+// order. The decoder reads, at each check, one word for every lane whose plane-0
+// state fell below 2^16 (lane order), then one for every plane-1 state. Encoding
+// runs backwards, so words are pushed in the mirrored order and reversed at the end.
+//
+// Renormalisation rule (proof sketch): with M = 2^8 and I = [2^16, 2^32), the
+// states x that encode the pair (a then b in decode order) into I form the
+// interval [fa*fb, 2^16*fa*fb); for a single symbol, [2^8*f, 2^24*f). So the
+// encoder emits one 16-bit word exactly when x >= 2^16*fa*fb (resp. 2^24*f).
+void encode_ans_block(const uint8_t* p0, const uint8_t* p1, uint32_t W, const PlaneTables& t,
+                      std::vector<uint8_t>* payload, uint32_t* nwords) {
+  uint32_t st[2][WS_LANES];
+  for (int p = 0; p < 2; ++p)
+    for (uint32_t l = 0; l < WS_LANES; ++l) st[p][l] = WS_RANS_L;
+  std::vector<uint16_t> rev;
+  rev.reserve(W + 64);
+  const uint32_t groups = (W + WS_GROUP_WORDS - 1) / WS_GROUP_WORDS;
+  const uint32_t checks = groups * 4;
+  for (uint32_t c = checks; c-- > 0;) {
+    const uint32_t g = c >> 2, jj = (c & 3u) * 2u;
+    for (int p = 1; p >= 0; --p) {
+      const uint8_t* sy = p ? p1 : p0;
+      const uint32_t* freq = t.freq[p];
+      const uint32_t* cdf = t.cdf[p];
+      for (int l = WS_LANES - 1; l >= 0; --l) {
+        const uint32_t ia = g * WS_GROUP_WORDS + (uint32_t)l * WS_WORDS_PER_LANE + jj;
+        if (ia >= W) continue;
+        const bool has_b = ia + 1 < W;
+        uint32_t x = st[p][l];
+        const uint32_t sa = sy[ia];
+        const uint32_t fa = freq[sa];
+        uint64_t xmax;
+        uint32_t sb = 0, fb = 0;
+        if (has_b) {
+          sb = sy[ia + 1];
+          fb = freq[sb];
+          xmax = ((uint64_t)fa * fb) << 16;
+        } else {
+          xmax = (uint64_t)fa << 24;
+        }
+        if ((uint64_t)x >= xmax) {
+          rev.push_back((uint16_t)(x & 0xFFFFu));
+          x >>= 16;
+        }
+        if (has_b) x = ((x / fb) << WS_PROB_BITS) + (x % fb) + cdf[sb];
+        x = ((x / fa) << WS_PROB_BITS) + (x % fa) + cdf[sa];
+        st[p][l] = x;
+      }
+    }
+  }
+  const uint32_t stream = (uint32_t)rev.size();
+  *nwords = WS_HEADER_HALFWORDS + stream;
+  const uint32_t bytes = round_up16(2u * *nwords);
+  payload->assign(bytes, 0);
+  uint8_t* out = payload->data();
+  for (int p = 0; p < 2; ++p)
+    for (uint32_t l = 0; l < WS_LANES; ++l) {
+      uint32_t v = st[p][l];
+      memcpy(out + 4 * (p * WS_LANES + l), &v, 4);
+    }
+  uint8_t* w = out + 2 * WS_HEADER_HALFWORDS;
+  for (uint32_t k = 0; k < stream; ++k) {
+    uint16_t v = rev[stream - 1 - k];
+    w[2 * k] = (uint8_t)(v & 0xFF);
+    w[2 * k + 1] = (uint8_t)(v >> 8);
+  }
+}
+
+bool all_zero_xor(const uint8_t* a, const uint8_t* b, uint64_t n) {
+  uint64_t i = 0, acc = 0;
+  for (; i + 8 <= n; i += 8) {
+    uint64_t x, y;
+    memcpy(&x, a + i, 8);
+    memcpy(&y, b + i, 8);
+    acc |= x ^ y;
+    if (acc) return false;
+  }
+  for (; i < n; ++i) acc |= (uint64_t)(a[i] ^ b[i]);
+  return acc == 0;
+}
+
+// Candidate encoding of one packet with the given symbol transform.
+struct Candidate {
+  uint64_t size = 0;
+  uint32_t table[512];
+  std::vector<EncodedBlock> blocks;
+};
+
+template <bool U16>
+void build_candidate(const uint8_t* base, const uint8_t* target, uint64_t n, const std::vector<uint8_t>& nonzero,
+                     Candidate* cand) {
+  const uint64_t W = n / 2;  // coded words; an odd last byte is carried raw in the block's tail field
+  uint64_t counts[2][256];
+  memset(counts, 0, sizeof(counts));
+  const uint32_t nblk = (uint32_t)((n + WS_BLOCK_BYTES - 1) / WS_BLOCK_BYTES);
+  for (uint32_t k = 0; k < nblk; ++k) {
+    if (!nonzero[k]) continue;
+    const uint64_t w0 = (uint64_t)k * (WS_BLOCK_BYTES / 2);
+    const uint64_t w1 = std::min<uint64_t>(W, w0 + WS_BLOCK_BYTES / 2);
+    for (uint64_t w = w0; w < w1; ++w) {
+      uint16_t v;
+      if (U16)
+        v = u16_symbol_word(load_u16(base + 2 * w), load_u16(target + 2 * w));
+      else
+        v = (uint16_t)(load_u16(base + 2 * w) ^ load_u16(target + 2 * w));
+      counts[0][v & 0xFF]++;
+      counts[1][v >> 8]++;
+    }
+  }
+  PlaneTables t;
+  tables_from_counts(counts, &t, cand->table);
+  cand->size = 1024;  // compact per-packet tables (2 x 256 frequencies of 9 bits, rounded)
+  std::vector<uint8_t> p0(WS_BLOCK_BYTES / 2), p1(WS_BLOCK_BYTES / 2);
+  for (uint32_t k = 0; k < nblk; ++k) {
+    if (!nonzero[k]) continue;
+    EncodedBlock blk;
+    blk.offset = k * WS_BLOCK_BYTES;
+    blk.nbytes = (uint32_t)std::min<uint64_t>(WS_BLOCK_BYTES, n - blk.offset);
+    blk.tail = 0;
+    blk.flags = 0;
+    const uint32_t wb = blk.nbytes / 2;
+    const uint8_t* bb = base + blk.offset;
+    const uint8_t* tb = target + blk.offset;
+    for (uint32_t w = 0; w < wb; ++w) {
+      uint16_t v;
+      if (U16)
+        v = u16_symbol_word(load_u16(bb + 2 * w), load_u16(tb + 2 * w));
+      else
+        v = (uint16_t)(load_u16(bb + 2 * w) ^ load_u16(tb + 2 * w));
+      p0[w] = (uint8_t)(v & 0xFF);
+      p1[w] = (uint8_t)(v >> 8);
+    }
+    if (blk.nbytes & 1u) {
+      blk.flags |= WS_FLAG_ODD_TAIL;
+      blk.tail = (uint8_t)(bb[blk.nbytes - 1] ^ tb[blk.nbytes - 1]);
+    }
+    encode_ans_block(p0.data(), p1.data(), wb, t, &blk.payload, &blk.nwords);
+    blk.kind = U16 ? WS_KIND_ANS_U16 : WS_KIND_ANS_XOR;
+    const uint32_t raw = round_up16(blk.nbytes);
+    if (blk.payload.size() >= raw) {  // incompressible block: carry its XOR bytes raw
+      blk.kind = WS_KIND_RAW;
+      blk.flags = 0;
+      blk.tail = 0;
+      blk.nwords = 0;
+      blk.payload.assign(raw, 0);
+      for (uint32_t i = 0; i < blk.nbytes; ++i) blk.payload[i] = (uint8_t)(bb[i] ^ tb[i]);
+    }
+    blk.lane_sum[0] = block_lane_sum(tb, blk.nbytes);
+    blk.lane_sum[1] = block_lane_sum(bb, blk.nbytes);
+    cand->size += blk.payload.size();
+    cand->blocks.push_back(std::move(blk));
+  }
+}
+
+}  // namespace
+
+void quantize_frequencies(const uint64_t counts[256], uint32_t f[256]) {
+  uint64_t total = 0;
+  int present = 0, last = 0;
+  for (int s = 0; s < 256; ++s) {
+    total += counts[s];
+    if (counts[s]) {
+      ++present;
+      last = s;
+    }
+    f[s] = 0;
+  }
+  if (present == 0) return;
+  if (present == 1) {
+    f[last] = WS_PROB_SCALE;
+    return;
+  }
+  int64_t sum = 0;
+  for (int s = 0; s < 256; ++s) {
+    if (!counts[s]) continue;
+    uint64_t v = (uint64_t)((unsigned __int128)counts[s] * WS_PROB_SCALE / total);
+    f[s] = v ? (uint32_t)v : 1u;
+    sum += f[s];
+  }
+  // Greedy fix-up: each +1/-1 step picks the symbol whose code length changes most/least.
+  while (sum < (int64_t)WS_PROB_SCALE) {
+    int best = -1;
+    double best_gain = -1.0;
+    for (int s = 0; s < 256; ++s) {
+      if (!counts[s]) continue;
+      double gain = (double)counts[s] * std::log2((double)(f[s] + 1) / (double)f[s]);
+      if (gain > best_gain) {
+        best_gain = gain;
+        best = s;
+      }
+    }
+    f[best]++;
+    ++sum;
+  }
+  while (sum > (int64_t)WS_PROB_SCALE) {
+    int best = -1;
+    double best_loss = 0.0;
+    for (int s = 0; s < 256; ++s) {
+      if (f[s] <= 1) continue;
+      double loss = (double)counts[s] * std::log2((double)f[s] / (double)(f[s] - 1));
+      if (best < 0 || loss < best_loss) {
+        best_loss = loss;
+        best = s;
+      }
+    }
+    f[best]--;
+    --sum;
+  }
+}
+
+void build_slot_entries(const uint32_t freqs[256], uint32_t entries[256]) {
+  uint32_t slot = 0;
+  for (uint32_t s = 0; s < 256; ++s)
+    for (uint32_t k = 0; k < freqs[s]; ++k, ++slot) entries[slot] = WS_ENTRY(k, s, freqs[s]);
+  for (; slot < 256; ++slot) entries[slot] = 0;  // only reachable for an empty table
+}
+
+void u16_residual_reference(const uint8_t* base, const uint8_t* target, uint64_t nbytes, uint8_t* out) {
+  const uint64_t W = nbytes / 2;
+  for (uint64_t w = 0; w < W; ++w) {
+    int32_t d = (int32_t)(int16_t)(uint16_t)(load_u16(target + 2 * w) - load_u16(base + 2 * w));
+    uint32_t z = ((uint32_t)(d * 2) ^ (uint32_t)(d >> 15)) & 0xFFFFu;
+    out[w] = (uint8_t)(z & 0xFF);
+    out[W + w] = (uint8_t)(z >> 8);
+  }
+}
+
+uint64_t block_lane_sum(const uint8_t* bytes, uint32_t n) {
+  const uint32_t groups = (n + WS_GROUP_BYTES - 1) / WS_GROUP_BYTES;
+  uint64_t sum = 0;
+  for (uint32_t l = 0; l < WS_LANES; ++l) {
+    uint32_t a = 0, b = 0;
+    for (uint32_t g = 0; g < groups; ++g) {
+      const uint32_t off = g * WS_GROUP_BYTES + l * 16u;
+      uint8_t chunk[16];
+      memset(chunk, 0, 16);
+      if (off < n) memcpy(chunk, bytes + off, std::min<uint32_t>(16u, n - off));
+      uint32_t w[4];
+      memcpy(w, chunk, 16);
+      a += w[0] + w[1] + w[2] + w[3];
+      b += a;
+    }
+    sum += ws_lane_hash(a, b, l);
+  }
+  return sum;
+}
+
+void encode_packet(const uint8_t* base, const uint8_t* target, uint64_t n, bool is_bf16, int policy,
+                   EncodedPacket* out) {
+  out->nbytes = n;
+  out->blocks.clear();
+  out->zero_block_bytes = 0;
+  out->payload_bytes = 0;
+  if (n == 0 || all_zero_xor(base, target, n)) {
+    out->mode = WS_MODE_SKIP;
+    return;
+  }
+  const uint32_t nblk = (uint32_t)((n + WS_BLOCK_BYTES - 1) / WS_BLOCK_BYTES);
+  std::vector<uint8_t> nonzero(nblk);
+  for (uint32_t k = 0; k < nblk; ++k) {
+    const uint64_t off = (uint64_t)k * WS_BLOCK_BYTES;
+    const uint64_t len = std::min<uint64_t>(WS_BLOCK_BYTES, n - off);
+    nonzero[k] = !all_zero_xor(base + off, target + off, len);
+    if (!nonzero[k]) out->zero_block_bytes += len;
+  }
+  // delta.py:184: raw XOR is the default; its size is the packet size.
+  int mode = WS_MODE_XOR_RAW;
+  uint64_t best = n;
+  Candidate chosen;
+  const bool big = n >= WS_COMPRESS_MIN;  // delta.py:185
+  const bool try_xor = big && !(policy == 2 && is_bf16);
+  const bool try_u16 = big && is_bf16 && (n % 2 == 0) && policy != 1;
+  if (try_xor) {
+    Candidate c;
+    build_candidate<false>(base, target, n, nonzero, &c);
+    if (c.size < best) {  // delta.py:188-189: strictly smaller replaces raw
+      best = c.size;
+      mode = (n % 2 == 0) ? WS_MODE_XOR_GROUP2_ANS : WS_MODE_XOR_ANS;
+      chosen = std::move(c);
+    }
+  }
+  if (try_u16) {
+    Candidate c;
+    build_candidate<true>(base, target, n, nonzero, &c);
+    if (c.size < best) {  // delta.py:192-193: strictly smaller than the current best
+      best = c.size;
+      mode = WS_MODE_U16_ANS;
+      chosen = std::move(c);
+    }
+  }
+  out->mode = mode;
+  out->payload_bytes = best;
+  if (mode == WS_MODE_XOR_RAW) {
+    memset(out->table, 0, sizeof(out->table));
+    for (uint32_t k = 0; k < nblk; ++k) {
+      if (!nonzero[k]) continue;
+      EncodedBlock blk;
+      blk.offset = k * WS_BLOCK_BYTES;
+      blk.nbytes = (uint32_t)std::min<uint64_t>(WS_BLOCK_BYTES, n - blk.offset);
+      blk.kind = WS_KIND_RAW;
+      blk.tail = 0;
+      blk.flags = 0;
+      blk.nwords = 0;
+      blk.payload.assign(round_up16(blk.nbytes), 0);
+      const uint8_t* bb = base + blk.offset;
+      const uint8_t* tb = target + blk.offset;
+      for (uint32_t i = 0; i < blk.nbytes; ++i) blk.payload[i] = (uint8_t)(bb[i] ^ tb[i]);
+      blk.lane_sum[0] = block_lane_sum(tb, blk.nbytes);
+      blk.lane_sum[1] = block_lane_sum(bb, blk.nbytes);
+      out->blocks.push_back(std::move(blk));
+    }
+  } else {
+    memcpy(out->table, chosen.table, sizeof(out->table));
+    out->blocks = std::move(chosen.blocks);
+  }
+}
+
+}  // namespace ws

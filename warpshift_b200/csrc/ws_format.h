@@ -1,0 +1,119 @@
+// Delta stream format shared by the host encoder (ws_encoder.cpp) and the
+// sm_100a decode+apply kernel (ws_apply.cu).
+//
+// What the stream represents follows warpshift/delta.py of the reference:
+//   * a tensor is cut into packets of at most 16 MiB (delta.py:20 _CHUNK_BYTES),
+//     each with one mode chosen by delta.py:176-194 _encode_chunk:
+//       0 XOR_RAW, 1 XOR_GROUP2_ANS, 2 XOR_ANS (odd size), 3 U16_ANS, or SKIP
+//       when the packet's XOR is all zero (delta.py:181-182, 209-212);
+//   * applying XOR modes computes dst ^= residual, U16 mode computes
+//     dst = dst +/- unzigzag(residual) modulo 2^16 (delta.py:74-92).
+// The entropy stage is this project's own chunked, interleaved rANS code,
+// which replaces nvCOMP's ANS (delta.py:111-113, 164-174, 313-316):
+//   * a packet is cut into blocks of 64 KiB of weight bytes; one warp decodes
+//     one block; 32 lanes x 2 interleaved 32-bit states (plane 0 = low byte of
+//     each uint16 word, plane 1 = high byte) share one 16-bit renormalisation
+//     word stream;
+//   * per packet there is one 256-slot (8-bit precision) frequency table per
+//     plane, expanded into 32-bit slot entries;
+//   * a lane owns words 8*lane .. 8*lane+7 of every 256-word (512-byte) group,
+//     so after 8 decode steps it holds exactly one aligned 16-byte vector;
+//   * states are checked for renormalisation after every second decode step;
+//     with 8-bit precision two symbols lower a state by at most 2^16, so one
+//     16-bit read per check restores it.
+#pragma once
+#include <stdint.h>
+
+#define WS_PACKET_BYTES (16u << 20)  // delta.py:20
+#define WS_BLOCK_BYTES 65536u        // rANS chunk; one warp per block
+#define WS_COMPRESS_MIN 16384u       // delta.py:185 (compression tried only at >= 16384 B)
+#define WS_GROUP_WORDS 256u          // one 512-byte group per warp step of 8 words/lane
+#define WS_GROUP_BYTES 512u
+#define WS_LANES 32u
+#define WS_WORDS_PER_LANE 8u         // words per lane per group
+#define WS_PROB_BITS 8u
+#define WS_PROB_SCALE 256u
+#define WS_RANS_L 65536u             // lower bound of the normalised state interval [2^16, 2^32)
+#define WS_HEADER_HALFWORDS 128u     // 64 initial states (uint32) at the start of an ANS payload
+#define WS_PAYLOAD_ALIGN 16u         // every payload starts and ends 16-byte aligned
+#define WS_TILE_BLOCKS 16u           // blocks per CTA tile (one per warp)
+#define WS_RING_BYTES 2048u          // per-warp staging ring in shared memory (2 halves)
+#define WS_RING_HALF_BYTES 1024u
+
+// Packet modes (delta.py:23 _MODES) plus SKIP.
+enum ws_mode { WS_MODE_XOR_RAW = 0, WS_MODE_XOR_GROUP2_ANS = 1, WS_MODE_XOR_ANS = 2, WS_MODE_U16_ANS = 3, WS_MODE_SKIP = 4 };
+
+// Block kinds (per 64 KiB block inside a packet). All-zero blocks are omitted.
+enum ws_kind { WS_KIND_RAW = 0, WS_KIND_ANS_XOR = 1, WS_KIND_ANS_U16 = 2 };
+#define WS_FLAG_ODD_TAIL 1u  // block's last byte (odd packet size) is not coded; its XOR value is `tail`
+
+// Device-side errors reported through ws_device_result.errors.
+#define WS_DEVERR_STATE 1u     // final rANS state != WS_RANS_L
+#define WS_DEVERR_LENGTH 2u    // stream words consumed != nwords
+#define WS_DEVERR_TIMEOUT 4u   // a bounded wait on a staging barrier gave up
+#define WS_DEVERR_KIND 8u      // unknown block kind
+
+// 32-byte block descriptor (resident in HBM for the plan's lifetime).
+typedef struct ws_block_desc {
+  uint64_t dst;      // absolute address of the block's first weight byte
+  uint64_t src;      // byte offset of the block payload inside the plan arena
+  uint32_t nbytes;   // weight bytes covered (1 .. 65536)
+  uint32_t clen;     // payload bytes (multiple of 16)
+  uint32_t nwords;   // ANS: stream halfwords incl. the 128-halfword state header; RAW: 0
+  uint16_t kind;     // ws_kind
+  uint8_t tail;      // XOR value of the last byte when flags & WS_FLAG_ODD_TAIL
+  uint8_t flags;
+} ws_block_desc;
+
+// 16-byte tile descriptor: up to 16 blocks of one packet, one CTA.
+typedef struct ws_tile_desc {
+  uint32_t first_block;
+  uint32_t nblocks;
+  uint32_t table;  // packet table index (512 entries each), or WS_NO_TABLE
+  uint32_t pad;
+} ws_tile_desc;
+#define WS_NO_TABLE 0xFFFFFFFFu
+
+// Slot entry of a decode table: bits 0-7 bias = slot - cdf[sym], bits 8-15 sym,
+// bits 16-24 freq (1..256).
+#define WS_ENTRY(bias, sym, freq) ((uint32_t)(bias) | ((uint32_t)(sym) << 8) | ((uint32_t)(freq) << 16))
+
+// Accumulators written by the kernel for one apply.
+typedef struct ws_device_result {
+  unsigned long long checksum;  // sum of per-block hashes of the written bytes
+  uint32_t errors;              // OR of WS_DEVERR_*
+  uint32_t bad_block_plus1;     // 1 + index of a failing block, 0 if none
+} ws_device_result;
+
+// ---------------------------------------------------------------------------
+// Checksum of written bytes. For each block and each lane l, over the block's
+// 512-byte groups g in order, with w0..w3 the four little-endian uint32 words
+// of bytes [512g + 16l, 512g + 16l + 16) after the write (bytes past the block
+// end read as 0):  a += w0 + w1 + w2 + w3;  b += a   (mod 2^32).
+// lane hash h_l = mix64(((uint64)b << 32 | a) + (l + 1) * K1),
+// block hash = mix64(sum_l h_l ^ ((block_index + 1) * K2)); the plan checksum
+// is the sum of block hashes (mod 2^64) over all blocks written.
+// mix64 is the splitmix64 finaliser (Steele, Lea, Flood 2014).
+#define WS_CK_K1 0x9E3779B97F4A7C15ull
+#define WS_CK_K2 0xD1B54A32D192ED03ull
+
+#ifdef __CUDACC__
+#define WS_HD __host__ __device__ __forceinline__
+#else
+#define WS_HD static inline
+#endif
+
+WS_HD uint64_t ws_mix64(uint64_t x) {
+  x ^= x >> 30;
+  x *= 0xBF58476D1CE4E5B9ull;
+  x ^= x >> 27;
+  x *= 0x94D049BB133111EBull;
+  x ^= x >> 31;
+  return x;
+}
+WS_HD uint64_t ws_lane_hash(uint32_t a, uint32_t b, uint32_t lane) {
+  return ws_mix64((((uint64_t)b << 32) | a) + (uint64_t)(lane + 1) * WS_CK_K1);
+}
+WS_HD uint64_t ws_block_hash(uint64_t lane_sum, uint64_t block_index) {
+  return ws_mix64(lane_sum ^ ((block_index + 1) * WS_CK_K2));
+}

@@ -1,0 +1,20 @@
+// Launch helpers for the sm_100a kernels in ws_apply.cu.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ws_format.h"
+
+namespace ws {
+
+// Shared memory used by one CTA of the decode+apply kernel.
+size_t apply_smem_bytes();
+
+// One launch over tiles [tile_begin, tile_begin + ntiles). `payload` is the
+// device address of arena byte `payload_offset` (a staging slot or the resident
+// copy); block descriptors hold arena offsets.
+cudaError_t launch_apply(const ws_tile_desc* tiles, uint32_t tile_begin, uint32_t ntiles,
+                         const ws_block_desc* blocks, const uint32_t* tables, const uint8_t* payload,
+                         uint64_t payload_offset, ws_device_result* result, int reverse, cudaStream_t stream);
+
+}  // namespace ws

@@ -1,0 +1,621 @@
+// Host runtime behind the C ABI (include/warpshift_b200.h): prepare pipeline,
+// stream layout, device upload and the staged apply.
+//
+// Prepare follows warpshift/delta.py:196-280 (walk tensors in dict order in
+// 16 MiB packets, D2H each packet, choose a mode, pack a host arena and bounded
+// batches), but packets are copied device->host through a ring of pinned staging
+// buffers while a pool of host threads encodes them.
+// Apply follows delta.py:294-327 (copy stream + compute stream, event-chained
+// slots, blocking sync at the end), with one fused kernel per batch.
+#include <cuda_runtime.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <condition_variable>
+#include <deque>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/warpshift_b200.h"
+#include "ws_encoder.h"
+#include "ws_format.h"
+#include "ws_kernels.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+#define WS_CUDA_TRY(expr)                                                                             \
+  do {                                                                                                \
+    cudaError_t e_ = (expr);                                                                          \
+    if (e_ != cudaSuccess) return fail(WS_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+struct Batch {
+  uint32_t tile_begin, tile_end;
+  uint64_t arena_off, bytes;
+};
+
+struct PacketRef {
+  uint32_t tensor;
+  uint64_t offset, nbytes;
+};
+
+int default_threads() {
+  unsigned n = std::thread::hardware_concurrency();
+  return n ? (int)n : 1;
+}
+
+// Run fn(i) for i in [0, n) on `threads` threads.
+template <class F>
+void parallel_for(uint64_t n, int threads, F fn) {
+  if (n == 0) return;
+  threads = (int)std::min<uint64_t>((uint64_t)std::max(1, threads), n);
+  std::atomic<uint64_t> next{0};
+  auto body = [&]() {
+    for (uint64_t i = next++; i < n; i = next++) fn(i);
+  };
+  std::vector<std::thread> pool;
+  for (int t = 1; t < threads; ++t) pool.emplace_back(body);
+  body();
+  for (auto& t : pool) t.join();
+}
+
+}  // namespace
+
+struct ws_plan {
+  ws_build_options opts{};
+  int device = -1;
+  std::vector<ws_block_desc> blocks;
+  std::vector<ws_tile_desc> tiles;
+  std::vector<uint32_t> tables;
+  std::vector<Batch> batches;
+  uint8_t* arena = nullptr;
+  uint64_t arena_bytes = 0;
+  bool arena_pinned = false;
+  ws_plan_stats stats{};
+
+  bool uploaded = false;
+  ws_block_desc* d_blocks = nullptr;
+  ws_tile_desc* d_tiles = nullptr;
+  uint32_t* d_tables = nullptr;
+  std::vector<uint8_t*> d_slots;
+  uint64_t slot_bytes = 0;
+  uint8_t* d_resident = nullptr;
+  ws_device_result* d_result = nullptr;
+  ws_device_result* h_result = nullptr;
+  std::vector<cudaEvent_t> copy_done, compute_done;
+  cudaEvent_t start_event = nullptr;
+  cudaStream_t own_copy_stream = nullptr;
+
+  int pending_reverse = -1;
+  uint64_t pending_h2d = 0;
+  uint32_t pending_launches = 0;
+};
+
+namespace {
+
+void release_device(ws_plan* p) {
+  if (p->device < 0) return;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(p->device);
+  cudaFree(p->d_blocks);
+  cudaFree(p->d_tiles);
+  cudaFree(p->d_tables);
+  for (auto s : p->d_slots) cudaFree(s);
+  cudaFree(p->d_resident);
+  cudaFree(p->d_result);
+  if (p->h_result) cudaFreeHost(p->h_result);
+  for (auto e : p->copy_done) cudaEventDestroy(e);
+  for (auto e : p->compute_done) cudaEventDestroy(e);
+  if (p->start_event) cudaEventDestroy(p->start_event);
+  if (p->own_copy_stream) cudaStreamDestroy(p->own_copy_stream);
+  p->d_blocks = nullptr;
+  p->d_tiles = nullptr;
+  p->d_tables = nullptr;
+  p->d_slots.clear();
+  p->d_resident = nullptr;
+  p->d_result = nullptr;
+  p->h_result = nullptr;
+  p->copy_done.clear();
+  p->compute_done.clear();
+  p->start_event = nullptr;
+  p->own_copy_stream = nullptr;
+  p->uploaded = false;
+  if (prev >= 0) cudaSetDevice(prev);
+}
+
+void release_host(ws_plan* p) {
+  if (p->arena) {
+    if (p->arena_pinned)
+      cudaFreeHost(p->arena);
+    else
+      free(p->arena);
+  }
+  p->arena = nullptr;
+}
+
+// Encode all packets. Device targets go through a ring of pinned staging
+// buffers: the calling thread issues D2H copies in packet order, workers wait
+// on each copy's event and encode.
+int encode_all(const ws_tensor_desc* tensors, const std::vector<PacketRef>& packets, const ws_build_options& o,
+               cudaStream_t stream, std::vector<ws::EncodedPacket>* out) {
+  const int threads = o.threads > 0 ? o.threads : default_threads();
+  out->resize(packets.size());
+  if (!o.target_on_device) {
+    parallel_for(packets.size(), threads, [&](uint64_t i) {
+      const PacketRef& pr = packets[i];
+      const ws_tensor_desc& t = tensors[pr.tensor];
+      ws::encode_packet((const uint8_t*)t.base + pr.offset, (const uint8_t*)t.target + pr.offset, pr.nbytes,
+                        t.is_bf16 != 0, o.policy, &(*out)[i]);
+    });
+    return WS_OK;
+  }
+  const size_t nbuf = std::min<size_t>(packets.size(), (size_t)std::max(2, 2 * threads));
+  uint64_t buf_bytes = 0;
+  for (auto& pr : packets) buf_bytes = std::max(buf_bytes, pr.nbytes);
+  std::vector<uint8_t*> bufs(nbuf, nullptr);
+  std::vector<cudaEvent_t> events(nbuf, nullptr);
+  int rc = WS_OK;
+  for (size_t b = 0; b < nbuf && rc == WS_OK; ++b) {
+    if (cudaHostAlloc((void**)&bufs[b], buf_bytes, cudaHostAllocDefault) != cudaSuccess ||
+        cudaEventCreateWithFlags(&events[b], cudaEventDisableTiming) != cudaSuccess)
+      rc = fail(WS_ERR_NOMEM, "cannot allocate pinned staging for prepare");
+  }
+  std::mutex mu;
+  std::condition_variable cv;
+  std::deque<size_t> free_bufs;
+  std::deque<std::pair<size_t, size_t>> jobs;  // (packet, buffer)
+  bool done = false;
+  std::atomic<bool> worker_error{false};
+  for (size_t b = 0; b < nbuf; ++b) free_bufs.push_back(b);
+  auto worker = [&]() {
+    cudaSetDevice(o.device);
+    for (;;) {
+      std::pair<size_t, size_t> job;
+      {
+        std::unique_lock<std::mutex> lk(mu);
+        cv.wait(lk, [&] { return !jobs.empty() || done; });
+        if (jobs.empty()) return;
+        job = jobs.front();
+        jobs.pop_front();
+      }
+      const PacketRef& pr = packets[job.first];
+      const ws_tensor_desc& t = tensors[pr.tensor];
+      if (cudaEventSynchronize(events[job.second]) != cudaSuccess) {
+        worker_error = true;
+      } else {
+        ws::encode_packet((const uint8_t*)t.base + pr.offset, bufs[job.second], pr.nbytes, t.is_bf16 != 0,
+                          o.policy, &(*out)[job.first]);
+      }
+      {
+        std::lock_guard<std::mutex> lk(mu);
+        free_bufs.push_back(job.second);
+      }
+      cv.notify_all();
+    }
+  };
+  std::vector<std::thread> pool;
+  if (rc == WS_OK)
+    for (int t = 0; t < threads; ++t) pool.emplace_back(worker);
+  for (size_t i = 0; i < packets.size() && rc == WS_OK; ++i) {
+    size_t b;
+    {
+      std::unique_lock<std::mutex> lk(mu);
+      cv.wait(lk, [&] { return !free_bufs.empty(); });
+      b = free_bufs.front();
+      free_bufs.pop_front();
+    }
+    const PacketRef& pr = packets[i];
+    const uint8_t* src = (const uint8_t*)tensors[pr.tensor].target + pr.offset;
+    cudaError_t e = cudaMemcpyAsync(bufs[b], src, pr.nbytes, cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaEventRecord(events[b], stream);
+    if (e != cudaSuccess) {
+      rc = fail(WS_ERR_CUDA, std::string("prepare D2H: ") + cudaGetErrorString(e));
+      std::lock_guard<std::mutex> lk(mu);
+      free_bufs.push_back(b);
+      break;
+    }
+    {
+      std::lock_guard<std::mutex> lk(mu);
+      jobs.emplace_back(i, b);
+    }
+    cv.notify_all();
+  }
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    done = true;
+  }
+  cv.notify_all();
+  for (auto& t : pool) t.join();
+  for (size_t b = 0; b < nbuf; ++b) {
+    if (bufs[b]) cudaFreeHost(bufs[b]);
+    if (events[b]) cudaEventDestroy(events[b]);
+  }
+  if (rc == WS_OK && worker_error) rc = fail(WS_ERR_CUDA, "prepare: waiting for a D2H copy failed");
+  return rc;
+}
+
+int layout(ws_plan* p, const ws_tensor_desc* tensors, const std::vector<PacketRef>& packets,
+           std::vector<ws::EncodedPacket>& enc) {
+  ws_plan_stats& st = p->stats;
+  std::vector<uint64_t> packet_first_block(enc.size());
+  uint64_t arena = 0;
+  for (size_t i = 0; i < enc.size(); ++i) {
+    ws::EncodedPacket& e = enc[i];
+    const PacketRef& pr = packets[i];
+    st.mode_counts[e.mode]++;
+    st.packets++;
+    if (e.mode == WS_MODE_SKIP) {
+      st.skipped_bytes += pr.nbytes;
+      continue;
+    }
+    st.payload_bytes += e.payload_bytes;
+    st.zero_block_bytes += e.zero_block_bytes;
+    uint32_t table = WS_NO_TABLE;
+    if (e.mode != WS_MODE_XOR_RAW) {
+      table = (uint32_t)(p->tables.size() / 512);
+      p->tables.insert(p->tables.end(), e.table, e.table + 512);
+    }
+    packet_first_block[i] = p->blocks.size();
+    const uint64_t base_addr = (uint64_t)(uintptr_t)tensors[pr.tensor].target + pr.offset;
+    for (size_t k = 0; k < e.blocks.size(); ++k) {
+      const ws::EncodedBlock& b = e.blocks[k];
+      if (k % WS_TILE_BLOCKS == 0) {
+        ws_tile_desc t;
+        t.first_block = (uint32_t)p->blocks.size();
+        t.nblocks = (uint32_t)std::min<size_t>(WS_TILE_BLOCKS, e.blocks.size() - k);
+        t.table = table;
+        t.pad = 0;
+        p->tiles.push_back(t);
+      }
+      ws_block_desc d;
+      d.dst = base_addr + b.offset;
+      d.src = arena;
+      d.nbytes = b.nbytes;
+      d.clen = (uint32_t)b.payload.size();
+      d.nwords = b.nwords;
+      d.kind = b.kind;
+      d.tail = b.tail;
+      d.flags = b.flags;
+      const uint64_t index = p->blocks.size();
+      st.expected_checksum[0] += ws_block_hash(b.lane_sum[0], index);
+      st.expected_checksum[1] += ws_block_hash(b.lane_sum[1], index);
+      st.touched_bytes += b.nbytes;
+      p->blocks.push_back(d);
+      arena += b.payload.size();
+    }
+  }
+  if (p->blocks.size() > 0xFFFFFFFFull) return fail(WS_ERR_INVALID, "too many blocks in one plan");
+  // Batches: contiguous tile ranges whose payload fits one staging slot.
+  const uint64_t limit = p->opts.batch_bytes;
+  Batch cur{0, 0, 0, 0};
+  bool open = false;
+  for (uint32_t t = 0; t < p->tiles.size(); ++t) {
+    const ws_tile_desc& td = p->tiles[t];
+    const ws_block_desc& first = p->blocks[td.first_block];
+    const ws_block_desc& last = p->blocks[td.first_block + td.nblocks - 1];
+    const uint64_t bytes = last.src + last.clen - first.src;  // tiles are contiguous in the arena
+    if (open && cur.bytes + bytes > limit) {
+      p->batches.push_back(cur);
+      open = false;
+    }
+    if (!open) {
+      cur = Batch{t, t, first.src, 0};
+      open = true;
+    }
+    cur.tile_end = t + 1;
+    cur.bytes += bytes;
+  }
+  if (open) p->batches.push_back(cur);
+  // Arena: every payload, in block order.
+  p->arena_bytes = arena;
+  if (arena) {
+    if (p->opts.pin_arena) {
+      if (cudaHostAlloc((void**)&p->arena, arena, cudaHostAllocDefault) != cudaSuccess)
+        return fail(WS_ERR_NOMEM, "cannot allocate the pinned delta arena");
+      p->arena_pinned = true;
+    } else {
+      if (posix_memalign((void**)&p->arena, 4096, arena) != 0) return fail(WS_ERR_NOMEM, "cannot allocate arena");
+    }
+    const int threads = p->opts.threads > 0 ? p->opts.threads : default_threads();
+    parallel_for(enc.size(), threads, [&](uint64_t i) {
+      if (enc[i].mode == WS_MODE_SKIP) return;
+      uint64_t first = packet_first_block[i];
+      for (size_t k = 0; k < enc[i].blocks.size(); ++k) {
+        const auto& pl = enc[i].blocks[k].payload;
+        memcpy(p->arena + p->blocks[first + k].src, pl.data(), pl.size());
+      }
+    });
+  }
+  st.arena_bytes = arena;
+  st.table_bytes = p->tables.size() * 4;
+  st.metadata_bytes = p->blocks.size() * sizeof(ws_block_desc) + p->tiles.size() * sizeof(ws_tile_desc) +
+                      st.table_bytes;
+  st.blocks = p->blocks.size();
+  st.tiles = p->tiles.size();
+  st.batches = p->batches.size();
+  return WS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ws_version(void) { return 100; }
+
+int ws_last_error(char* buf, size_t len) {
+  if (!buf || len == 0) return WS_ERR_INVALID;
+  size_t n = std::min(len - 1, g_last_error.size());
+  memcpy(buf, g_last_error.data(), n);
+  buf[n] = 0;
+  return WS_OK;
+}
+
+int ws_u16_residual(const uint8_t* base, const uint8_t* target, uint64_t nbytes, uint8_t* out) {
+  if (nbytes % 2) return fail(WS_ERR_INVALID, "U16 residual needs an even byte count");
+  if (nbytes && (!base || !target || !out)) return fail(WS_ERR_INVALID, "null pointer");
+  ws::u16_residual_reference(base, target, nbytes, out);
+  return WS_OK;
+}
+
+int ws_plan_build(const ws_tensor_desc* tensors, uint64_t ntensors, const ws_build_options* opts, void* stream,
+                  ws_plan** out) {
+  if (!out || !opts || (ntensors && !tensors)) return fail(WS_ERR_INVALID, "null argument");
+  *out = nullptr;
+  if (opts->policy < WS_POLICY_AUTO || opts->policy > WS_POLICY_U16) return fail(WS_ERR_INVALID, "unknown policy");
+  const auto started = std::chrono::steady_clock::now();
+  ws_plan* p = new (std::nothrow) ws_plan();
+  if (!p) return fail(WS_ERR_NOMEM, "out of memory");
+  p->opts = *opts;
+  if (p->opts.batch_bytes == 0) p->opts.batch_bytes = 16ull << 20;
+  if (p->opts.batch_bytes < (2ull << 20)) {
+    delete p;
+    return fail(WS_ERR_INVALID, "batch_bytes must be at least 2 MiB");
+  }
+  if (p->opts.staging_slots <= 0) p->opts.staging_slots = 3;
+  p->device = opts->target_on_device ? opts->device : -1;
+  // Destination spans must not overlap (delta.py:159-162).
+  std::vector<std::pair<uint64_t, uint64_t>> spans;
+  for (uint64_t i = 0; i < ntensors; ++i) {
+    const ws_tensor_desc& t = tensors[i];
+    if (t.nbytes && (!t.base || !t.target)) {
+      delete p;
+      return fail(WS_ERR_INVALID, "tensor " + std::to_string(i) + " has a null pointer");
+    }
+    if (t.nbytes) spans.emplace_back((uint64_t)(uintptr_t)t.target, (uint64_t)(uintptr_t)t.target + t.nbytes);
+  }
+  std::sort(spans.begin(), spans.end());
+  for (size_t i = 1; i < spans.size(); ++i)
+    if (spans[i].first < spans[i - 1].second) {
+      delete p;
+      return fail(WS_ERR_INVALID, "Delta cannot update overlapping tensors");
+    }
+  std::vector<PacketRef> packets;
+  for (uint64_t i = 0; i < ntensors; ++i)
+    for (uint64_t off = 0; off < tensors[i].nbytes; off += WS_PACKET_BYTES)
+      packets.push_back(PacketRef{(uint32_t)i, off, std::min<uint64_t>(WS_PACKET_BYTES, tensors[i].nbytes - off)});
+  for (uint64_t i = 0; i < ntensors; ++i) p->stats.runtime_bytes += tensors[i].nbytes;
+  int prev = -1;
+  if (opts->target_on_device) {
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(opts->device) != cudaSuccess) {
+      delete p;
+      return fail(WS_ERR_CUDA, "cannot select device " + std::to_string(opts->device));
+    }
+  }
+  std::vector<ws::EncodedPacket> enc;
+  int rc = encode_all(tensors, packets, p->opts, (cudaStream_t)stream, &enc);
+  if (rc == WS_OK) rc = layout(p, tensors, packets, enc);
+  if (prev >= 0) cudaSetDevice(prev);
+  if (rc != WS_OK) {
+    release_host(p);
+    delete p;
+    return rc;
+  }
+  p->stats.encode_seconds =
+      std::chrono::duration<double>(std::chrono::steady_clock::now() - started).count();
+  *out = p;
+  return WS_OK;
+}
+
+int ws_plan_upload(ws_plan* p, void* stream) {
+  if (!p) return fail(WS_ERR_INVALID, "null plan");
+  if (p->device < 0) return fail(WS_ERR_STATE, "plan was built for host targets; nothing to upload");
+  if (p->uploaded) return WS_OK;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  WS_CUDA_TRY(cudaSetDevice(p->device));
+  cudaStream_t s = (cudaStream_t)stream;
+  auto alloc_copy = [&](void** dst, const void* src, size_t bytes) -> cudaError_t {
+    if (!bytes) return cudaSuccess;
+    cudaError_t e = cudaMalloc(dst, bytes);
+    if (e != cudaSuccess) return e;
+    return cudaMemcpyAsync(*dst, src, bytes, cudaMemcpyHostToDevice, s);
+  };
+  cudaError_t e = alloc_copy((void**)&p->d_blocks, p->blocks.data(), p->blocks.size() * sizeof(ws_block_desc));
+  if (e == cudaSuccess) e = alloc_copy((void**)&p->d_tiles, p->tiles.data(), p->tiles.size() * sizeof(ws_tile_desc));
+  if (e == cudaSuccess) e = alloc_copy((void**)&p->d_tables, p->tables.data(), p->tables.size() * 4);
+  if (e == cudaSuccess) e = cudaMalloc((void**)&p->d_result, sizeof(ws_device_result));
+  if (e == cudaSuccess) e = cudaHostAlloc((void**)&p->h_result, sizeof(ws_device_result), cudaHostAllocDefault);
+  uint64_t slot = 0;
+  for (auto& b : p->batches) slot = std::max(slot, b.bytes);
+  p->slot_bytes = slot;
+  const int nslots = p->batches.empty() ? 0 : std::min<int>(p->opts.staging_slots, (int)p->batches.size());
+  for (int i = 0; i < nslots && e == cudaSuccess; ++i) {
+    uint8_t* d = nullptr;
+    e = cudaMalloc((void**)&d, slot);
+    if (e == cudaSuccess) p->d_slots.push_back(d);
+    cudaEvent_t a = nullptr, b = nullptr;
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&a, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&b, cudaEventDisableTiming);
+    if (a) p->copy_done.push_back(a);
+    if (b) p->compute_done.push_back(b);
+  }
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->start_event, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p->own_copy_stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) {
+    std::string msg = std::string("upload: ") + cudaGetErrorString(e);
+    release_device(p);
+    if (prev >= 0) cudaSetDevice(prev);
+    return fail(e == cudaErrorMemoryAllocation ? WS_ERR_NOMEM : WS_ERR_CUDA, msg);
+  }
+  p->stats.scratch_bytes = (uint64_t)nslots * slot + sizeof(ws_device_result);
+  p->uploaded = true;
+  if (prev >= 0) cudaSetDevice(prev);
+  return WS_OK;
+}
+
+int ws_plan_set_resident(ws_plan* p, int resident, void* stream) {
+  if (!p) return fail(WS_ERR_INVALID, "null plan");
+  if (!p->uploaded) return fail(WS_ERR_STATE, "upload the plan first");
+  int prev = -1;
+  cudaGetDevice(&prev);
+  WS_CUDA_TRY(cudaSetDevice(p->device));
+  if (resident && !p->d_resident && p->arena_bytes) {
+    cudaError_t e = cudaMalloc((void**)&p->d_resident, p->arena_bytes);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(p->d_resident, p->arena, p->arena_bytes, cudaMemcpyHostToDevice, (cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+    if (e != cudaSuccess) {
+      cudaFree(p->d_resident);
+      p->d_resident = nullptr;
+      if (prev >= 0) cudaSetDevice(prev);
+      return fail(WS_ERR_CUDA, std::string("resident copy: ") + cudaGetErrorString(e));
+    }
+    p->stats.scratch_bytes += p->arena_bytes;
+  } else if (!resident && p->d_resident) {
+    cudaFree(p->d_resident);
+    p->d_resident = nullptr;
+    p->stats.scratch_bytes -= p->arena_bytes;
+  }
+  if (prev >= 0) cudaSetDevice(prev);
+  return WS_OK;
+}
+
+int ws_apply_async(ws_plan* p, int reverse, void* compute_stream, void* copy_stream) {
+  if (!p) return fail(WS_ERR_INVALID, "null plan");
+  if (!p->uploaded) return fail(WS_ERR_STATE, "upload the plan before applying");
+  reverse = reverse ? 1 : 0;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  WS_CUDA_TRY(cudaSetDevice(p->device));
+  cudaStream_t comp = (cudaStream_t)compute_stream;
+  cudaStream_t copy = copy_stream ? (cudaStream_t)copy_stream : p->own_copy_stream;
+  uint64_t h2d = 0;
+  uint32_t launches = 0;
+  WS_CUDA_TRY(cudaMemsetAsync(p->d_result, 0, sizeof(ws_device_result), comp));
+  if (p->d_resident || p->arena_bytes == 0) {
+    if (!p->tiles.empty()) {
+      WS_CUDA_TRY(ws::launch_apply(p->d_tiles, 0, (uint32_t)p->tiles.size(), p->d_blocks, p->d_tables,
+                                   p->d_resident, 0, p->d_result, reverse, comp));
+      launches = 1;
+    }
+  } else {
+    const size_t nslots = p->d_slots.size();
+    WS_CUDA_TRY(cudaEventRecord(p->start_event, comp));
+    WS_CUDA_TRY(cudaStreamWaitEvent(copy, p->start_event, 0));
+    for (size_t b = 0; b < p->batches.size(); ++b) {
+      const Batch& bt = p->batches[b];
+      const size_t slot = b % nslots;
+      if (b >= nslots) WS_CUDA_TRY(cudaStreamWaitEvent(copy, p->compute_done[slot], 0));
+      WS_CUDA_TRY(cudaMemcpyAsync(p->d_slots[slot], p->arena + bt.arena_off, bt.bytes, cudaMemcpyHostToDevice, copy));
+      WS_CUDA_TRY(cudaEventRecord(p->copy_done[slot], copy));
+      WS_CUDA_TRY(cudaStreamWaitEvent(comp, p->copy_done[slot], 0));
+      WS_CUDA_TRY(ws::launch_apply(p->d_tiles, bt.tile_begin, bt.tile_end - bt.tile_begin, p->d_blocks, p->d_tables,
+                                   p->d_slots[slot], bt.arena_off, p->d_result, reverse, comp));
+      WS_CUDA_TRY(cudaEventRecord(p->compute_done[slot], comp));
+      h2d += bt.bytes;
+      ++launches;
+    }
+  }
+  WS_CUDA_TRY(cudaMemcpyAsync(p->h_result, p->d_result, sizeof(ws_device_result), cudaMemcpyDeviceToHost, comp));
+  p->pending_reverse = reverse;
+  p->pending_h2d = h2d;
+  p->pending_launches = launches;
+  if (prev >= 0) cudaSetDevice(prev);
+  return WS_OK;
+}
+
+int ws_apply_finish(ws_plan* p, void* compute_stream, ws_apply_result* out) {
+  if (!p) return fail(WS_ERR_INVALID, "null plan");
+  if (p->pending_reverse < 0) return fail(WS_ERR_STATE, "no apply in flight");
+  int prev = -1;
+  cudaGetDevice(&prev);
+  WS_CUDA_TRY(cudaSetDevice(p->device));
+  cudaError_t e = cudaStreamSynchronize((cudaStream_t)compute_stream);
+  if (prev >= 0) cudaSetDevice(prev);
+  const int reverse = p->pending_reverse;
+  p->pending_reverse = -1;
+  if (e != cudaSuccess) return fail(WS_ERR_CUDA, std::string("apply: ") + cudaGetErrorString(e));
+  ws_apply_result r{};
+  r.checksum = p->h_result->checksum;
+  r.expected = p->stats.expected_checksum[reverse];
+  r.device_errors = p->h_result->errors;
+  r.bad_block_plus1 = p->h_result->bad_block_plus1;
+  r.h2d_bytes = p->pending_h2d;
+  r.launches = p->pending_launches;
+  if (out) *out = r;
+  if (r.device_errors) {
+    char msg[160];
+    snprintf(msg, sizeof(msg), "delta decode failed: device errors 0x%x at block %u", r.device_errors,
+             r.bad_block_plus1 ? r.bad_block_plus1 - 1 : 0);
+    return fail(WS_ERR_DEVICE, msg);
+  }
+  if (r.checksum != r.expected) {
+    char msg[200];
+    snprintf(msg, sizeof(msg),
+             "delta apply checksum mismatch (got %016llx, expected %016llx): resident weights were not the "
+             "expected source model",
+             (unsigned long long)r.checksum, (unsigned long long)r.expected);
+    return fail(WS_ERR_CHECKSUM, msg);
+  }
+  return WS_OK;
+}
+
+int ws_apply(ws_plan* p, int reverse, void* compute_stream, void* copy_stream, ws_apply_result* out) {
+  int rc = ws_apply_async(p, reverse, compute_stream, copy_stream);
+  if (rc != WS_OK) return rc;
+  return ws_apply_finish(p, compute_stream, out);
+}
+
+int ws_plan_get_stats(const ws_plan* p, ws_plan_stats* out) {
+  if (!p || !out) return fail(WS_ERR_INVALID, "null argument");
+  *out = p->stats;
+  return WS_OK;
+}
+
+int ws_plan_get_view(const ws_plan* p, ws_plan_view* out) {
+  if (!p || !out) return fail(WS_ERR_INVALID, "null argument");
+  out->blocks = p->blocks.data();
+  out->nblocks = p->blocks.size();
+  out->tiles = p->tiles.data();
+  out->ntiles = p->tiles.size();
+  out->tables = p->tables.data();
+  out->ntables = p->tables.size() / 512;
+  out->arena = p->arena;
+  out->arena_bytes = p->arena_bytes;
+  return WS_OK;
+}
+
+void ws_plan_destroy(ws_plan* p) {
+  if (!p) return;
+  release_device(p);
+  release_host(p);
+  delete p;
+}
+
+}  // extern "C"
