@@ -30,7 +30,7 @@ constexpr uint32_t kBarOffset = kRingOffset + kWarps * WS_RING_BYTES;
 constexpr uint32_t kSmemBytes = kBarOffset + kWarps * 2 * 8;
 constexpr uint32_t kRingHalfwords = WS_RING_BYTES / 2;      // 1024
 constexpr uint32_t kHalfHalfwords = WS_RING_HALF_BYTES / 2; // 512
-constexpr uint32_t kWaitLimit = 1u << 22;                   // bounded spin on a staging barrier
+constexpr uint32_t kWaitLimit = 1u << 20;                   // bounded spin on a staging barrier
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
