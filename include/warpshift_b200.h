@@ -140,6 +140,26 @@ WS_API int ws_apply_finish(ws_plan* plan, void* compute_stream, ws_apply_result*
 WS_API int ws_plan_get_stats(const ws_plan* plan, ws_plan_stats* out);
 WS_API int ws_plan_get_view(const ws_plan* plan, ws_plan_view* out);
 
+/* No counterpart in the reference. Allocation-free apply for callers that cannot
+ * let a library call cudaMalloc (an engine whose KV-cache pool already holds all
+ * free HBM, or one that routes every device allocation through its own
+ * allocator). The caller passes, in device memory on `device`, the tile and
+ * block descriptors and slot tables of a plan (layouts of ws_plan_get_view) and
+ * the whole payload arena (block `src` offsets are relative to `payload`); the
+ * weights named by the block descriptors are written in place and `out`
+ * receives the checksum and device errors (`out->expected` stays 0: compare
+ * with ws_plan_stats.expected_checksum). Its only scratch is a fixed
+ * 16-byte-per-tile device array of WS_NOALLOC_MAX_TILES + 1 slots (256 KiB)
+ * inside the library, held by every GPU that loads the library until exit; more
+ * than WS_NOALLOC_MAX_TILES tiles per call is rejected with WS_ERR_INVALID.
+ * The first call on a device looks up that array's device address (module
+ * set-up), so make it before any stream capture. All calls on a device share the
+ * array: calls that overlap on the GPU race and must be serialised by the
+ * caller. Synchronous: returns after `stream` completes. */
+#define WS_NOALLOC_MAX_TILES 16384
+WS_API int ws_apply_device_noalloc(const void* tiles, uint32_t ntiles, const void* blocks, const uint32_t* tables,
+                                   const void* payload, int reverse, int device, void* stream, ws_apply_result* out);
+
 /* Frees host and device resources (delta.py relies on GC for the same). */
 WS_API void ws_plan_destroy(ws_plan* plan);
 

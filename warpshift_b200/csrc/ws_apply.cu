@@ -382,3 +382,193 @@ cudaError_t launch_apply(const ws_tile_desc* tiles, uint32_t tile_begin, uint32_
 }
 
 }  // namespace ws
+
+// ---------------------------------------------------------------------------
+// Allocation-free apply (ws_apply_device_noalloc in include/warpshift_b200.h).
+//
+// Some callers cannot let a library call cudaMalloc at switch time: a serving
+// engine that has already handed all free HBM to its KV-cache pool, or one that
+// owns every device allocation through its own allocator. This entry point
+// takes descriptors, tables and payload that the caller already placed in
+// device memory, writes the weights in place, and keeps its only scratch (one
+// result slot per tile plus one total) in the fixed array below, which every
+// GPU that loads this library holds until the process exits.
+#include <mutex>
+#include <string>
+
+#include "../../include/warpshift_b200.h"
+
+static __device__ __align__(256) ws_device_result g_noalloc_scratch[WS_NOALLOC_MAX_TILES + 1];
+
+namespace ws {
+namespace {
+
+// Same per-tile work as ws_apply_kernel, but each tile accumulates into its own
+// scratch slot (slot = tile index) instead of one shared accumulator.
+template <bool REVERSE>
+__global__ void __launch_bounds__(kThreads, 2)
+    ws_apply_noalloc_kernel(const ws_tile_desc* __restrict__ tiles, const ws_block_desc* __restrict__ blocks,
+                            const uint32_t* __restrict__ tables, const uint8_t* __restrict__ payload,
+                            ws_device_result* scratch) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint32_t* tbl = reinterpret_cast<uint32_t*>(smem);
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  const ws_tile_desc tile = tiles[blockIdx.x];
+  ws_device_result* res = scratch + blockIdx.x;
+  if (tile.table != WS_NO_TABLE) {
+    const uint32_t t = threadIdx.x;
+    const uint32_t e = __ldg(tables + (uint64_t)tile.table * 512u + t);
+    const uint4 v = make_uint4(e, e, e, e);
+    uint4* row = reinterpret_cast<uint4*>(tbl + (t >> 8) * kTableWords + (t & 255u) * 32u);
+#pragma unroll
+    for (uint32_t k = 0; k < 8; ++k) row[(k + t) & 7u] = v;
+  }
+  const uint32_t bar_base = smem_addr(smem + kBarOffset) + warp * 16u;
+  if (lane == 0) {
+    mbar_init(bar_base, 1);
+    mbar_init(bar_base + 8, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (warp >= tile.nblocks) return;
+  const uint32_t block = tile.first_block + warp;
+  const ws_block_desc bd = blocks[block];
+  const uint8_t* src = payload + bd.src;
+  uint8_t* ring = smem + kRingOffset + warp * WS_RING_BYTES;
+  switch (bd.kind) {
+    case WS_KIND_RAW:
+      raw_block(bd, block, src, lane, res);
+      break;
+    case WS_KIND_ANS_XOR:
+      ans_block<false, REVERSE>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
+      break;
+    case WS_KIND_ANS_U16:
+      ans_block<true, REVERSE>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
+      break;
+    default:
+      if (lane == 0) report(res, WS_DEVERR_KIND, block);
+  }
+}
+
+// Sums the per-tile slots [0, n) into slot WS_NOALLOC_MAX_TILES (one CTA).
+__global__ void ws_noalloc_reduce_kernel(ws_device_result* scratch, uint32_t n) {
+  __shared__ unsigned long long sum[256];
+  __shared__ uint32_t err[256], bad[256];
+  unsigned long long s = 0;
+  uint32_t e = 0, b = 0;
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+    s += scratch[i].checksum;
+    e |= scratch[i].errors;
+    if (scratch[i].bad_block_plus1) b = scratch[i].bad_block_plus1;
+  }
+  sum[threadIdx.x] = s;
+  err[threadIdx.x] = e;
+  bad[threadIdx.x] = b;
+  __syncthreads();
+  for (uint32_t stride = blockDim.x / 2; stride > 0; stride >>= 1) {
+    if (threadIdx.x < stride) {
+      sum[threadIdx.x] += sum[threadIdx.x + stride];
+      err[threadIdx.x] |= err[threadIdx.x + stride];
+      if (!bad[threadIdx.x]) bad[threadIdx.x] = bad[threadIdx.x + stride];
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    scratch[WS_NOALLOC_MAX_TILES].checksum = sum[0];
+    scratch[WS_NOALLOC_MAX_TILES].errors = err[0];
+    scratch[WS_NOALLOC_MAX_TILES].bad_block_plus1 = bad[0];
+  }
+}
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+ws_device_result* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on `device` (which must be current).
+// Host code cannot use the symbol itself: it names a host-side shadow.
+int noalloc_scratch(int device, ws_device_result** out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mutex);
+  if (!g_noalloc_ptr[device]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+      set_last_error((std::string("cudaGetSymbolAddress(no-alloc scratch): ") + cudaGetErrorString(e)).c_str());
+      return WS_ERR_CUDA;
+    }
+    g_noalloc_ptr[device] = static_cast<ws_device_result*>(p);
+  }
+  *out = g_noalloc_ptr[device];
+  return WS_OK;
+}
+
+}  // namespace
+}  // namespace ws
+
+extern "C" WS_API int ws_apply_device_noalloc(const void* tiles, uint32_t ntiles, const void* blocks,
+                                              const uint32_t* tables, const void* payload, int reverse, int device,
+                                              void* stream, ws_apply_result* out) {
+  using namespace ws;
+  if (!out) {
+    set_last_error("ws_apply_device_noalloc: null result pointer");
+    return WS_ERR_INVALID;
+  }
+  *out = ws_apply_result{};
+  if (ntiles == 0) return WS_OK;
+  if (ntiles > WS_NOALLOC_MAX_TILES) {
+    set_last_error(("ws_apply_device_noalloc: " + std::to_string(ntiles) + " tiles exceed the maximum of " +
+                    std::to_string(WS_NOALLOC_MAX_TILES) +
+                    " per call (its per-tile results live in a fixed device array); split the tiles over several calls")
+                       .c_str());
+    return WS_ERR_INVALID;
+  }
+  if (!tiles || !blocks || !payload || device < 0 || device >= kMaxDevices) {
+    set_last_error("ws_apply_device_noalloc: null descriptor/payload pointer or bad device ordinal");
+    return WS_ERR_INVALID;
+  }
+  int prev = -1;
+  cudaGetDevice(&prev);
+  auto done = [&](int rc) {
+    if (prev >= 0) cudaSetDevice(prev);
+    return rc;
+  };
+  cudaError_t e = cudaSetDevice(device);
+  ws_device_result* scratch = nullptr;
+  if (e != cudaSuccess) {
+    set_last_error((std::string("ws_apply_device_noalloc: ") + cudaGetErrorString(e)).c_str());
+    return done(WS_ERR_CUDA);
+  }
+  int rc = noalloc_scratch(device, &scratch);
+  if (rc != WS_OK) return done(rc);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto kernel = reverse ? ws_apply_noalloc_kernel<true> : ws_apply_noalloc_kernel<false>;
+  // The slots used by this call start at zero; the array keeps the previous call's values otherwise.
+  e = cudaMemsetAsync(scratch, 0, sizeof(ws_device_result) * ntiles, s);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+  if (e == cudaSuccess) {
+    kernel<<<ntiles, kThreads, kSmemBytes, s>>>(static_cast<const ws_tile_desc*>(tiles),
+                                                 static_cast<const ws_block_desc*>(blocks), tables,
+                                                 static_cast<const uint8_t*>(payload), scratch);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) {
+    ws_noalloc_reduce_kernel<<<1, 256, 0, s>>>(scratch, ntiles);
+    e = cudaGetLastError();
+  }
+  ws_device_result total{};
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(&total, scratch + WS_NOALLOC_MAX_TILES, sizeof(total), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) {
+    set_last_error((std::string("ws_apply_device_noalloc: ") + cudaGetErrorString(e)).c_str());
+    return done(WS_ERR_CUDA);
+  }
+  out->checksum = total.checksum;
+  out->device_errors = total.errors;
+  out->bad_block_plus1 = total.bad_block_plus1;
+  out->launches = 2;
+  if (total.errors) {
+    set_last_error("ws_apply_device_noalloc: device reported a corrupt block");
+    return done(WS_ERR_DEVICE);
+  }
+  return done(WS_OK);
+}

@@ -17,4 +17,7 @@ cudaError_t launch_apply(const ws_tile_desc* tiles, uint32_t tile_begin, uint32_
                          const ws_block_desc* blocks, const uint32_t* tables, const uint8_t* payload,
                          uint64_t payload_offset, ws_device_result* result, int reverse, cudaStream_t stream);
 
+// Records the message returned by ws_last_error() on the calling thread.
+void set_last_error(const char* msg);
+
 }  // namespace ws

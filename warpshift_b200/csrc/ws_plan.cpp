@@ -74,6 +74,11 @@ void parallel_for(uint64_t n, int threads, F fn) {
 
 }  // namespace
 
+namespace ws {
+// Lets entry points defined in other translation units record ws_last_error().
+void set_last_error(const char* msg) { g_last_error = msg; }
+}  // namespace ws
+
 struct ws_plan {
   ws_build_options opts{};
   int device = -1;
