@@ -53,6 +53,8 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline time budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--threads", type=int, default=0, help="host encoder threads (0 = all)")
+    p.add_argument("--layers", type=int, default=0, help="truncate the model to N layers (small profiling cases)")
+    p.add_argument("--skip-e2e", action="store_true", help="time only the kernel-only switch (profiling cases)")
     return p.parse_args()
 
 
@@ -140,13 +142,20 @@ def init_distributed(args):
 
 
 def workload_spec(args, world: int, rank: int):
+    import dataclasses
+
     from warpshift_b200 import synth
 
+    shape = synth.SHAPES[args.workload]
+    suffix = ""
+    if args.layers:
+        shape = dataclasses.replace(shape, layers=min(args.layers, shape.layers))
+        suffix = f", truncated to {shape.layers} layers"
     if args.workload == "llama3-70b":
-        return synth.model_spec("llama3-70b", tp=world, rank=rank), f"llama3-70b tp={world} rank shard"
+        return synth.model_spec(shape, tp=world, rank=rank), f"llama3-70b tp={world} rank shard{suffix}"
     if args.workload == "mixtral-8x7b":
-        return synth.model_spec("mixtral-8x7b", tp=8, rank=rank % 8), "mixtral-8x7b tp=8 shard per rank"
-    return synth.model_spec(args.workload), f"{args.workload} tp=1 per rank"
+        return synth.model_spec(shape, tp=8, rank=rank % 8), f"mixtral-8x7b tp=8 shard per rank{suffix}"
+    return synth.model_spec(shape), f"{args.workload} tp=1 per rank{suffix}"
 
 
 def generate_on_device(spec, device, scale):
@@ -339,7 +348,7 @@ def run_ours(args) -> None:
     C = int(native.arena_bytes)
     touched = int(native.touched_bytes)
     meta = int(native.metadata_bytes)
-    h2d_gbs = measure_h2d(device)
+    h2d_gbs = measure_h2d(device) if not args.skip_e2e else float("nan")
     stream = delta.compute_stream
 
     def barrier():
@@ -396,33 +405,34 @@ def run_ours(args) -> None:
         delta.set_resident(False)
 
         # ---- end to end through DeltaWeights.apply: H2D staging + result read-back each step
-        for _ in range(args.warmup):
-            delta.apply(reverse=state_is_b)
-            if group is not None:
-                delta.confirm(group)
-            state_is_b = not state_is_b
-        launches_e = 0
-        barrier()
-        caller = torch.cuda.current_stream(device)
-        e_begin, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e_begin.record(caller)
-        for k in range(args.steps):
-            delta.apply(reverse=state_is_b)
-            if group is not None:
-                delta.confirm(group)
-            launches_e += delta.last_apply["launches"]
-            state_is_b = not state_is_b
-        e_end.record(caller)
-        torch.cuda.synchronize(device)
-        barrier()
-        e2e_ms = e_begin.elapsed_time(e_end)
+        e2e_ms, launches_e = None, 0
+        if not args.skip_e2e:
+            for _ in range(args.warmup):
+                delta.apply(reverse=state_is_b)
+                if group is not None:
+                    delta.confirm(group)
+                state_is_b = not state_is_b
+            barrier()
+            caller = torch.cuda.current_stream(device)
+            e_begin, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e_begin.record(caller)
+            for k in range(args.steps):
+                delta.apply(reverse=state_is_b)
+                if group is not None:
+                    delta.confirm(group)
+                launches_e += delta.last_apply["launches"]
+                state_is_b = not state_is_b
+            e_end.record(caller)
+            torch.cuda.synchronize(device)
+            barrier()
+            e2e_ms = e_begin.elapsed_time(e_end)
     clocks = sampler.summary()
 
     kernel_ms_max = max_over_ranks(kernel_ms)
-    e2e_ms_max = max_over_ranks(e2e_ms)
+    e2e_ms_max = max_over_ranks(e2e_ms) if e2e_ms is not None else None
     W_total = sum_over_ranks(W)
     value = W_total * args.steps / (kernel_ms_max * 1e-3) / 1e9
-    e2e_value = W_total * args.steps / (e2e_ms_max * 1e-3) / 1e9
+    e2e_value = W_total * args.steps / (e2e_ms_max * 1e-3) / 1e9 if e2e_ms_max else None
     avg_step_ms = statistics.mean(step_ms)
     algo_bytes = 2 * touched + C + meta
     achieved = algo_bytes / (avg_step_ms * 1e-3) / 1e9
@@ -433,7 +443,7 @@ def run_ours(args) -> None:
         entry = json.loads(traffic_file.read_text()).get(f"{args.workload}/{args.policy}/{args.scale}")
         if entry:
             traffic = entry["dram_bytes_per_launch"]
-    t_roof_ms = max(C / (h2d_gbs * 1e9), algo_bytes / (pk["hbm_gbs"] * 1e9)) * 1e3
+    t_roof_ms = max(C / (h2d_gbs * 1e9) if h2d_gbs == h2d_gbs else 0.0, algo_bytes / (pk["hbm_gbs"] * 1e9)) * 1e3
     # Exactness check of the final state against a regenerated Teacher (first and last tensor).
     from warpshift_b200 import synth
 
@@ -473,7 +483,7 @@ def run_ours(args) -> None:
             "parallelism": f"{world} independent rank shard(s), NCCL checksum all-reduce per switch" if world > 1 else "1 GPU",
             "kernel_step_ms": [round(x, 3) for x in step_ms],
         },
-        "e2e": {
+        "e2e": None if e2e_value is None else {
             "value": round(e2e_value, 2),
             "unit": UNIT,
             "ms_per_step": round(e2e_ms_max / args.steps, 3),

@@ -47,7 +47,7 @@ def edge_pair(seed: int = 0, scale: float = 0.01, big: bool = True) -> tuple[dic
     put("buffer:fp32_cache", f, f * (1 + 1e-3 * torch.from_numpy(rng.standard_normal(30001).astype(np.float32))))
     u = torch.from_numpy(rng.integers(0, 256, 50001, dtype=np.uint8))
     v = u.clone()
-    v[::5] ^= torch.from_numpy(rng.integers(1, 256, v[::5].numel(), dtype=np.uint8))
+    v[::5] ^= torch.from_numpy(rng.integers(1, 4, v[::5].numel(), dtype=np.uint8))  # small change alphabet
     put("buffer:u8_odd", u, v)
     u = torch.from_numpy(rng.integers(0, 256, 16383, dtype=np.uint8))
     put("buffer:u8_16383", u, u ^ 1)

@@ -1,0 +1,37 @@
+"""The C-ABI library loads without a GPU and exports every symbol include/warpshift_b200.h declares."""
+
+from __future__ import annotations
+
+import re
+import subprocess
+from pathlib import Path
+
+from warpshift_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "warpshift_b200.h"
+
+
+def declared() -> set[str]:
+    return set(re.findall(r"^WS_API\s+(?:int|void)\s+(ws_\w+)\s*\(", HEADER.read_text(), flags=re.M))
+
+
+def test_header_declares_the_api() -> None:
+    names = declared()
+    assert {"ws_plan_build", "ws_plan_upload", "ws_apply", "ws_last_error", "ws_plan_destroy"} <= names
+
+
+def test_library_exports_every_declared_symbol() -> None:
+    lib = _lib.load()
+    for name in declared():
+        assert hasattr(lib, name), name
+    assert declared() == set(_lib.SIGNATURES), "ctypes signatures must cover exactly the header"
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIBRARY)], capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r" T (ws_\w+)", out))
+    assert exported == declared(), "the library must export exactly the declared ABI"
+
+
+def test_version_and_error_buffer_without_a_gpu() -> None:
+    lib = _lib.load()
+    assert lib.ws_version() >= 100
+    assert lib.ws_u16_residual(None, None, 3, None) == _lib.WS_ERR_INVALID
+    assert "even" in _lib.last_error()

@@ -1,0 +1,159 @@
+"""Host encoder (product) checked by the oracle's independent C decoder, on CPU.
+
+Plans are built on host targets, so every byte the encoder emits is decoded by
+oracle/stream_oracle.c and applied to host copies; results must equal Teacher1 /
+Teacher2 bit-exactly and the oracle's checksum must equal the one recorded at
+prepare. The U16 representation is pinned to the reference residual
+(delta.py:26-34): coded word = rotr16(zigzag(d), 1).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import semantics as sem
+from oracle import stream as ostream
+from tests.helpers import as_bytes, bf16_pair, edge_pair, host_plan, plan_arrays
+from warpshift_b200 import _lib
+
+KIND_RAW, KIND_XOR, KIND_U16 = 0, 1, 2
+
+
+def clone(d):
+    return {k: v.clone() for k, v in d.items()}
+
+
+@pytest.mark.parametrize("policy", ["auto", "xor", "u16"])
+def test_host_plan_round_trips_through_the_oracle_decoder(policy: str) -> None:
+    a, b = edge_pair(seed=7)
+    work = clone(b)
+    plan = host_plan(a, work, policy)
+    try:
+        blocks, tiles, tables, arena, stats = plan_arrays(plan)
+        assert stats.runtime_bytes == sum(t.numel() * t.element_size() for t in b.values())
+        for reverse, teacher in ((True, a), (False, b), (True, a)):
+            err, checksum = ostream.apply_plan(blocks, tiles, tables, arena, 0, reverse, 4)
+            assert err == 0
+            assert checksum == stats.expected_checksum[1 if reverse else 0]
+            for name in b:
+                np.testing.assert_array_equal(as_bytes(work[name]), as_bytes(teacher[name]), err_msg=name)
+    finally:
+        _lib.load().ws_plan_destroy(plan)
+
+
+def test_mode_rule_follows_the_reference() -> None:
+    """delta.py:176-194: <16384 B raw, unchanged SKIP, odd sizes XOR_ANS, XOR-only policy never U16."""
+    a, b = edge_pair(seed=8)
+    expected_skipped = sum(x.numel() * x.element_size() for n, x in a.items() if torch.equal(x, b[n]))
+    for policy in ("auto", "xor", "u16"):
+        plan = host_plan(a, clone(b), policy)
+        *_, stats = plan_arrays(plan)
+        counts = dict(zip(_lib.MODE_NAMES, list(stats.mode_counts)))
+        assert counts["SKIP"] == 1 and stats.skipped_bytes == expected_skipped
+        small = sum(1 for n, x in b.items() if 0 < x.numel() * x.element_size() < sem.COMPRESS_MIN and not torch.equal(x, a[n]))
+        assert counts["XOR_RAW"] >= small
+        if policy == "xor":
+            assert counts["U16_ANS"] == 0 and counts["XOR_GROUP2_ANS"] > 0
+        else:
+            assert counts["U16_ANS"] > 0
+        assert counts["XOR_ANS"] >= 1  # the odd-sized compressible uint8 tensor
+        _lib.load().ws_plan_destroy(plan)
+
+
+@pytest.mark.parametrize("policy", ["xor", "u16"])
+def test_coded_words_are_the_reference_residual(policy: str) -> None:
+    a_t, b_t = bf16_pair(3 * 32768 + 1000, 0.01, 9)
+    a, b = {"w": a_t}, {"w": b_t.clone()}
+    plan = host_plan(a, b, policy)
+    try:
+        blocks, tiles, tables, arena, stats = plan_arrays(plan)
+        base, target = as_bytes(a_t), as_bytes(b_t)
+        xor_words = sem.xor_residual(base, target).view("<u2")
+        z = sem.u16_residual(base, target)
+        half = z.size // 2
+        zig = z[:half].astype(np.uint32) | (z[half:].astype(np.uint32) << 8)
+        rot = ((zig >> 1) | ((zig & 1) << 15)).astype("<u2")
+        t = tiles[0]
+        table = tables[512 * t["table"] : 512 * t["table"] + 512]
+        for i, blk in enumerate(blocks):
+            if blk["kind"] == KIND_RAW:
+                continue
+            payload = arena[blk["src"] : blk["src"] + blk["clen"]]
+            words, err = ostream.decode_words(payload, blk, table)
+            assert err == 0
+            w0 = (int(blk["dst"]) - b["w"].data_ptr()) // 2
+            ref = (rot if blk["kind"] == KIND_U16 else xor_words)[w0 : w0 + words.size]
+            np.testing.assert_array_equal(words, ref, err_msg=f"block {i}")
+            assert blk["kind"] == (KIND_U16 if policy == "u16" else KIND_XOR)
+    finally:
+        _lib.load().ws_plan_destroy(plan)
+
+
+def test_corrupt_payload_is_detected_by_the_final_state_check() -> None:
+    a_t, b_t = bf16_pair(40000, 0.01, 10)
+    work = {"w": b_t.clone()}
+    plan = host_plan({"w": a_t}, work, "xor")
+    try:
+        blocks, tiles, tables, arena, stats = plan_arrays(plan)
+        blk = next(bk for bk in blocks if bk["kind"] != KIND_RAW)
+        arena[blk["src"] + 300] ^= 0x40  # a renormalisation word
+        err, _ = ostream.apply_plan(blocks, tiles, tables, arena, 0, True, 1)
+        assert err & 3
+    finally:
+        _lib.load().ws_plan_destroy(plan)
+
+
+def test_overlapping_targets_and_bad_options_are_rejected() -> None:
+    lib = _lib.load()
+    buf = torch.zeros(1000, dtype=torch.uint8)
+    base = torch.zeros(1000, dtype=torch.uint8)
+    descs = (_lib.TensorDesc * 2)()
+    descs[0] = _lib.TensorDesc(base.data_ptr(), buf.data_ptr(), 600, 0, 0)
+    descs[1] = _lib.TensorDesc(base.data_ptr(), buf.data_ptr() + 500, 500, 0, 0)
+    opts = _lib.BuildOptions(policy=0, threads=1, target_on_device=0, device=0, batch_bytes=0, staging_slots=0, pin_arena=0)
+    plan = ctypes.c_void_p()
+    assert lib.ws_plan_build(descs, 2, ctypes.byref(opts), None, ctypes.byref(plan)) == _lib.WS_ERR_INVALID
+    assert "overlapping" in _lib.last_error()
+    opts.batch_bytes = 1 << 20
+    assert lib.ws_plan_build(descs, 1, ctypes.byref(opts), None, ctypes.byref(plan)) == _lib.WS_ERR_INVALID
+    opts.batch_bytes, opts.policy = 0, 9
+    assert lib.ws_plan_build(descs, 1, ctypes.byref(opts), None, ctypes.byref(plan)) == _lib.WS_ERR_INVALID
+    assert lib.ws_plan_upload(None, None) == _lib.WS_ERR_INVALID
+
+
+def test_host_plan_cannot_be_uploaded_or_applied() -> None:
+    a, b = {"w": torch.ones(10)}, {"w": torch.zeros(10)}
+    plan = host_plan(a, b, "auto")
+    lib = _lib.load()
+    try:
+        assert lib.ws_plan_upload(plan, None) == _lib.WS_ERR_STATE
+        res = _lib.ApplyResult()
+        assert lib.ws_apply(plan, 0, None, None, ctypes.byref(res)) == _lib.WS_ERR_STATE
+    finally:
+        lib.ws_plan_destroy(plan)
+
+
+def test_empty_and_fully_unchanged_models_have_nothing_to_apply() -> None:
+    x = torch.randn(50000)
+    plan = host_plan({"x": x, "e": torch.zeros(0)}, {"x": x.clone(), "e": torch.zeros(0)}, "auto")
+    blocks, tiles, tables, arena, stats = plan_arrays(plan)
+    assert stats.blocks == 0 and stats.arena_bytes == 0 and stats.skipped_bytes == x.numel() * 4
+    assert ostream.apply_plan(blocks, tiles, tables, np.zeros(1, np.uint8), 0, True, 1) == (0, 0)
+    _lib.load().ws_plan_destroy(plan)
+
+
+def test_high_entropy_blocks_fall_back_to_raw_and_stay_exact() -> None:
+    rng = np.random.default_rng(3)
+    u = torch.from_numpy(rng.integers(0, 256, 3 * 65536, dtype=np.uint8))
+    v = torch.from_numpy(rng.integers(0, 256, 3 * 65536, dtype=np.uint8))
+    work = {"u": v.clone()}
+    plan = host_plan({"u": u}, work, "auto")
+    blocks, tiles, tables, arena, stats = plan_arrays(plan)
+    assert all(bk["kind"] == KIND_RAW for bk in blocks)
+    assert ostream.apply_plan(blocks, tiles, tables, arena, 0, True, 2)[0] == 0
+    assert torch.equal(work["u"], u)
+    _lib.load().ws_plan_destroy(plan)

@@ -130,3 +130,35 @@ def test_misaligned_destinations(cuda_device) -> None:
         assert_bytes_equal(b, a)
         delta.apply(reverse=False)
         assert_bytes_equal(b, ref_b)
+
+
+def test_corrupt_frame_is_reported_and_the_context_stays_usable(cuda_device) -> None:
+    """Host-side fault injection: one flipped payload byte in the pinned arena.
+
+    The kernel's reads stay inside the staging ring and the block whatever the
+    bytes are, so a corrupt frame can only produce wrong values; the final rANS
+    state / stream length check reports it as a device error (no trap, no fault).
+    """
+    import ctypes
+
+    from oracle import stream as ostream
+
+    a, b = edge_pair(seed=5, big=False)
+    gpu = to_device(b, cuda_device)
+    delta = DeltaWeights(a, gpu, policy="xor")
+    view = delta.plan_view()
+    blocks = np.ctypeslib.as_array((ctypes.c_uint8 * (32 * view.nblocks)).from_address(view.blocks)).view(ostream.BLOCK_DTYPE)
+    arena = np.ctypeslib.as_array((ctypes.c_uint8 * view.arena_bytes).from_address(view.arena))
+    ans = [i for i, bk in enumerate(blocks) if bk["kind"] != 0]
+    assert ans
+    target = blocks[ans[0]]
+    arena[int(target["src"]) + 260] ^= 0x21  # a renormalisation word of the first ANS block
+    with pytest.raises(RuntimeError, match="decode failed"):
+        delta.apply(reverse=True)
+    assert delta.last_apply["device_errors"] & 3
+    arena[int(target["src"]) + 260] ^= 0x21
+    # Same context, fresh package: still exact.
+    gpu2 = to_device(b, cuda_device)
+    fresh = DeltaWeights(a, gpu2, policy="xor")
+    fresh.apply(reverse=True)
+    assert_bytes_equal(gpu2, a)
