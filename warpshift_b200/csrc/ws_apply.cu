@@ -11,7 +11,13 @@
 // replicated 32 times in shared memory so that lane l always reads bank l
 // (conflict-free random lookups). Each warp streams its compressed payload
 // from HBM into a 2 x 1 KiB shared-memory ring with cp.async.bulk (TMA bulk
-// copies, no multicast) completing on per-slot mbarriers.
+// copies, no multicast) completing on per-slot mbarriers; a mirror of the
+// first 640 bytes of each even half sits behind the ring so that a group's
+// reads never need wrapping.
+//
+// The inner loop (two decode steps of both planes plus the warp-cooperative
+// renormalisation) is hand-written PTX: about 50 instructions per 4 decoded
+// bytes per lane, balanced between the ALU and FMA pipes.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -26,13 +32,26 @@ constexpr uint32_t kWarps = WS_TILE_BLOCKS;
 constexpr uint32_t kThreads = kWarps * 32;
 constexpr uint32_t kTableWords = 256 * 32;                  // one replicated plane table
 constexpr uint32_t kRingOffset = 2 * kTableWords * 4;       // bytes
-constexpr uint32_t kBarOffset = kRingOffset + kWarps * WS_RING_BYTES;
+constexpr uint32_t kMirror = 640;  // a group reads <= 512 + 128 bytes past its start position
+constexpr uint32_t kRingStride = WS_RING_BYTES + kMirror;
+constexpr uint32_t kBarOffset = kRingOffset + kWarps * kRingStride;
 constexpr uint32_t kSmemBytes = kBarOffset + kWarps * 2 * 8;
 constexpr uint32_t kRingHalfwords = WS_RING_BYTES / 2;      // 1024
 constexpr uint32_t kHalfHalfwords = WS_RING_HALF_BYTES / 2; // 512
 constexpr uint32_t kWaitLimit = 1u << 20;                   // bounded spin on a staging barrier
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds16(uint32_t addr) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+  return v;
+}
 
 __device__ __forceinline__ uint32_t lanemask_lt() {
   uint32_t m;
@@ -57,6 +76,20 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
       "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// One expect_tx covering two bulk copies of the same source (ring slot + mirror).
+__device__ __forceinline__ void bulk_load2(uint32_t dst0, uint32_t dst1, const void* src, uint32_t bytes0,
+                                           uint32_t bytes1, uint32_t bar) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes0 + bytes1) : "memory");
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst0),
+      "l"(src), "r"(bytes0), "r"(bar)
+      : "memory");
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst1),
+      "l"(src), "r"(bytes1), "r"(bar)
       : "memory");
 }
 
@@ -174,26 +207,75 @@ __device__ void raw_block(const ws_block_desc& bd, uint32_t block, const uint8_t
   ck.finish(lane, block, res);
 }
 
-// Decode one step for both planes: word = sym0 | sym1 << 8.
-#define WS_DECODE_STEP(ea, eb)                                   \
-  {                                                              \
-    ea = tbl0[((xa & 255u) << 5) | lane];                        \
-    eb = tbl1[((xb & 255u) << 5) | lane];                        \
-    xa = (ea >> 16) * (xa >> 8) + (ea & 255u);                   \
-    xb = (eb >> 16) * (xb >> 8) + (eb & 255u);                   \
+// Generic-path decode step (partial groups, unaligned destinations): both
+// planes, word = sym0 | sym1 << 8. Slot entry: bias | sym << 8 | freq << 16.
+#define WS_STEP_C(ea, eb)                                      \
+  {                                                            \
+    ea = lds32(tb0 + ((xa & 255u) << 7));                      \
+    eb = lds32(tb1 + ((xb & 255u) << 7));                      \
+    xa = (ea >> 16) * (xa >> 8) + (ea & 255u);                 \
+    xb = (eb >> 16) * (xb >> 8) + (eb & 255u);                 \
   }
 
-// Renormalisation check: plane-0 reads first in lane order, then plane 1.
-#define WS_RENORM()                                                                   \
-  {                                                                                   \
-    const bool na = xa < WS_RANS_L, nb = xb < WS_RANS_L;                              \
-    const uint32_t ba = __ballot_sync(0xFFFFFFFFu, na);                               \
-    const uint32_t bb = __ballot_sync(0xFFFFFFFFu, nb);                               \
-    const uint32_t ca = __popc(ba);                                                   \
-    if (na) xa = (xa << 16) | ring16[(pos + __popc(ba & ltm)) & (kRingHalfwords - 1)]; \
-    if (nb) xb = (xb << 16) | ring16[(pos + ca + __popc(bb & ltm)) & (kRingHalfwords - 1)]; \
-    pos += ca + __popc(bb);                                                           \
+// Generic-path renormalisation: every state below 2^16 reads one word; plane-0
+// reads come first in lane order, then plane-1 reads.
+#define WS_RENORM_C()                                                                         \
+  {                                                                                           \
+    const uint32_t base = ring_s + (pos & (kRingHalfwords - 1)) * 2u;                         \
+    const bool na = xa < WS_RANS_L, nb = xb < WS_RANS_L;                                      \
+    const uint32_t ba = __ballot_sync(0xFFFFFFFFu, na);                                       \
+    const uint32_t bb = __ballot_sync(0xFFFFFFFFu, nb);                                       \
+    const uint32_t ca = __popc(ba);                                                           \
+    if (na) xa = (xa << 16) | lds16(base + 2u * __popc(ba & ltm));                            \
+    if (nb) xb = (xb << 16) | lds16(base + 2u * (ca + __popc(bb & ltm)));                     \
+    pos += ca + __popc(bb);                                                                   \
   }
+
+// Fast-path check in hand-written PTX: two decode steps of both planes (the
+// lane's words 2c and 2c+1 of the group) and one renormalisation check.
+// rp is the byte address of the current stream position in the ring; the
+// caller re-bases it once per group. Returns the two words as lo | hi << 16.
+__device__ __forceinline__ uint32_t check_fast(uint32_t& xa, uint32_t& xb, uint32_t& rp, uint32_t tb0, uint32_t tb1,
+                                               uint32_t ltm) {
+  uint32_t out;
+  asm volatile(
+      "{\n"
+      " .reg .u32 sa, sb, aa, ab, ea, eb, qa, qb, fa, fb, ba, bb, w0, w1, va, vb, ca, cb, oa, ob, t, ada, adb, wa, wb;\n"
+      " .reg .pred pa, pb;\n"
+      // step 1: slot -> replicated entry -> x' = freq * (x >> 8) + bias
+      " and.b32 sa, %0, 255;\n and.b32 sb, %1, 255;\n"
+      " mad.lo.u32 aa, sa, 128, %4;\n mad.lo.u32 ab, sb, 128, %5;\n"
+      " ld.shared.u32 ea, [aa];\n ld.shared.u32 eb, [ab];\n"
+      " shr.u32 qa, %0, 8;\n shr.u32 qb, %1, 8;\n"
+      " shr.u32 fa, ea, 16;\n shr.u32 fb, eb, 16;\n"
+      " and.b32 ba, ea, 255;\n and.b32 bb, eb, 255;\n"
+      " mad.lo.u32 %0, fa, qa, ba;\n mad.lo.u32 %1, fb, qb, bb;\n"
+      " prmt.b32 w0, ea, eb, 0x0051;\n"
+      // step 2
+      " and.b32 sa, %0, 255;\n and.b32 sb, %1, 255;\n"
+      " mad.lo.u32 aa, sa, 128, %4;\n mad.lo.u32 ab, sb, 128, %5;\n"
+      " ld.shared.u32 ea, [aa];\n ld.shared.u32 eb, [ab];\n"
+      " shr.u32 qa, %0, 8;\n shr.u32 qb, %1, 8;\n"
+      " shr.u32 fa, ea, 16;\n shr.u32 fb, eb, 16;\n"
+      " and.b32 ba, ea, 255;\n and.b32 bb, eb, 255;\n"
+      " mad.lo.u32 %0, fa, qa, ba;\n mad.lo.u32 %1, fb, qb, bb;\n"
+      " prmt.b32 w1, ea, eb, 0x5100;\n"
+      " prmt.b32 %2, w0, w1, 0x7610;\n"
+      // renormalisation: ballot, prefix counts, one 16-bit word per low state
+      " setp.lt.u32 pa, %0, 65536;\n setp.lt.u32 pb, %1, 65536;\n"
+      " vote.sync.ballot.b32 va, pa, 0xffffffff;\n vote.sync.ballot.b32 vb, pb, 0xffffffff;\n"
+      " popc.b32 ca, va;\n popc.b32 cb, vb;\n"
+      " and.b32 t, va, %6;\n popc.b32 oa, t;\n"
+      " and.b32 t, vb, %6;\n popc.b32 ob, t;\n add.u32 ob, ob, ca;\n"
+      " mad.lo.u32 ada, oa, 2, %3;\n mad.lo.u32 adb, ob, 2, %3;\n"
+      " @pa ld.shared.u16 wa, [ada];\n @pb ld.shared.u16 wb, [adb];\n"
+      " @pa prmt.b32 %0, wa, %0, 0x5410;\n @pb prmt.b32 %1, wb, %1, 0x5410;\n"
+      " add.u32 t, ca, cb;\n mad.lo.u32 %3, t, 2, %3;\n"
+      "}\n"
+      : "+r"(xa), "+r"(xb), "=r"(out), "+r"(rp)
+      : "r"(tb0), "r"(tb1), "r"(ltm));
+  return out;
+}
 
 template <bool U16, bool REVERSE>
 __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t* __restrict__ src,
@@ -208,14 +290,22 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
   const bool aligned = (bd.dst & 15u) == 0;
   const uint32_t total_halves = (bd.clen + WS_RING_HALF_BYTES - 1) / WS_RING_HALF_BYTES;
   const uint32_t ring_s = smem_addr(ring);
-  const uint16_t* ring16 = reinterpret_cast<const uint16_t*>(ring);
   const uint32_t ltm = lanemask_lt();
+  const uint32_t tb0 = smem_addr(tbl0) + lane * 4u, tb1 = smem_addr(tbl1) + lane * 4u;
 
+  // Half k of the payload goes to ring slot k & 1; even halves also refresh the
+  // mirror behind the ring end. Both copies complete on the slot's mbarrier.
   auto issue = [&](uint32_t k) {
     if (lane == 0 && k < total_halves) {
       const uint32_t off = k * WS_RING_HALF_BYTES;
       const uint32_t bytes = min(WS_RING_HALF_BYTES, bd.clen - off);
-      bulk_load(ring_s + (k & 1u) * WS_RING_HALF_BYTES, src + off, bytes, bar_base + (k & 1u) * 8u);
+      const uint32_t bar = bar_base + (k & 1u) * 8u;
+      if (k & 1u) {
+        bulk_load(ring_s + WS_RING_HALF_BYTES, src + off, bytes, bar);
+      } else {
+        const uint32_t mirror = min(kMirror, bytes);
+        bulk_load2(ring_s, ring_s + WS_RING_BYTES, src + off, bytes, mirror, bar);
+      }
     }
   };
   uint32_t issued = min(2u, total_halves);
@@ -232,71 +322,89 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
   uint32_t pos = WS_HEADER_HALFWORDS;
   Checksum ck;
 
-#pragma unroll 1
-  for (uint32_t g = 0; g < groups && ok; ++g) {
-    const uint32_t off = g * WS_GROUP_BYTES + lane * 16u;
-    const bool vec = aligned && (g + 1) * WS_GROUP_BYTES <= coded_bytes;
-    uint4 old = make_uint4(0, 0, 0, 0);
-    if (vec) old = *reinterpret_cast<const uint4*>(dst + off);
-    uint32_t r[4] = {0, 0, 0, 0};
-    if (g < dec_groups) {
-      // Recycle the slot whose half has been consumed, then make sure every
-      // halfword this group can read ([pos, pos + 256)) has landed.
-      while (issued < total_halves && pos >= kHalfHalfwords * (issued - 1)) {
-        __syncwarp();
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        issue(issued);
-        ++issued;
-      }
-      const uint32_t need = min(pos + 256u, bd.nwords);
-      while (ready < issued && need > kHalfHalfwords * ready) {
-        ok = mbar_wait(bar_base + (ready & 1u) * 8u, (ready >> 1) & 1u);
-        if (!ok) break;
-        ++ready;
-      }
-      if (!ok) break;
-      uint32_t ea0, eb0, ea1, eb1;
-      if ((g + 1) * WS_GROUP_WORDS <= W) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          WS_DECODE_STEP(ea0, eb0);
-          WS_DECODE_STEP(ea1, eb1);
-          r[c] = __byte_perm(__byte_perm(ea0, eb0, 0x0051), __byte_perm(ea1, eb1, 0x5100), 0x7610);
-          WS_RENORM();
-        }
-      } else {
-        const int first = (int)(g * WS_GROUP_WORDS + lane * WS_WORDS_PER_LANE);
-        const int valid = max(0, min(8, (int)W - first));
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          ea0 = eb0 = ea1 = eb1 = 0;
-          if (2 * c < valid) WS_DECODE_STEP(ea0, eb0);
-          if (2 * c + 1 < valid) WS_DECODE_STEP(ea1, eb1);
-          r[c] = __byte_perm(__byte_perm(ea0, eb0, 0x0051), __byte_perm(ea1, eb1, 0x5100), 0x7610);
-          WS_RENORM();
-        }
-      }
+  // Recycle the slot whose half has been consumed, then make sure every
+  // halfword the next group can read ([pos, pos + 256)) has landed.
+  auto stage = [&]() {
+    while (issued < total_halves && pos >= kHalfHalfwords * (issued - 1)) {
+      __syncwarp();
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(issued);
+      ++issued;
     }
-    if (vec) {
+    const uint32_t need = min(pos + 256u, bd.nwords);
+    while (ready < issued && need > kHalfHalfwords * ready) {
+      ok = mbar_wait(bar_base + (ready & 1u) * 8u, (ready >> 1) & 1u);
+      if (!ok) return;
+      ++ready;
+    }
+  };
+
+  // Fast path: full 512-byte groups of a 16-byte-aligned destination. The ring
+  // bookkeeping runs only when the stream position reaches `next_event`.
+  uint32_t g = 0;
+  const uint32_t fast_groups = aligned ? W / WS_GROUP_WORDS : 0;
+  {
+    uint32_t next_event = 0;
+    uint4* p = reinterpret_cast<uint4*>(dst + lane * 16u);
+#pragma unroll 1
+    for (; g < fast_groups; ++g, p += WS_GROUP_BYTES / 16) {
+      if (pos >= next_event) {
+        stage();
+        if (!ok) break;
+        const uint32_t recycle = issued < total_halves ? kHalfHalfwords * (issued - 1) : 0xFFFFFFFFu;
+        const uint32_t wait =
+            (ready < issued && bd.nwords > kHalfHalfwords * ready) ? kHalfHalfwords * ready - 255u : 0xFFFFFFFFu;
+        next_event = min(recycle, wait);
+      }
+      const uint4 old = *p;
+      uint32_t rp = ring_s + (pos & (kRingHalfwords - 1)) * 2u;
+      const uint32_t rp0 = rp;
+      const uint32_t r0 = check_fast(xa, xb, rp, tb0, tb1, ltm);
+      const uint32_t r1 = check_fast(xa, xb, rp, tb0, tb1, ltm);
+      const uint32_t r2 = check_fast(xa, xb, rp, tb0, tb1, ltm);
+      const uint32_t r3 = check_fast(xa, xb, rp, tb0, tb1, ltm);
+      pos += (rp - rp0) >> 1;
       uint4 v;
       if (U16) {
-        v.x = u16_apply(old.x, r[0], REVERSE);
-        v.y = u16_apply(old.y, r[1], REVERSE);
-        v.z = u16_apply(old.z, r[2], REVERSE);
-        v.w = u16_apply(old.w, r[3], REVERSE);
+        v.x = u16_apply(old.x, r0, REVERSE);
+        v.y = u16_apply(old.y, r1, REVERSE);
+        v.z = u16_apply(old.z, r2, REVERSE);
+        v.w = u16_apply(old.w, r3, REVERSE);
       } else {
-        v.x = old.x ^ r[0];
-        v.y = old.y ^ r[1];
-        v.z = old.z ^ r[2];
-        v.w = old.w ^ r[3];
+        v.x = old.x ^ r0;
+        v.y = old.y ^ r1;
+        v.z = old.z ^ r2;
+        v.w = old.w ^ r3;
       }
-      *reinterpret_cast<uint4*>(dst + off) = v;
+      *p = v;
       ck.add(v.x, v.y, v.z, v.w);
-    } else {
-      uint32_t out[4] = {0, 0, 0, 0};
-      apply_chunk_bytes<U16, REVERSE>(dst + off, off, n, r, coded_bytes, bd.tail, out);
-      ck.add(out[0], out[1], out[2], out[3]);
     }
+  }
+
+  // Generic path: the partial last group, the uncoded odd tail byte, and
+  // destinations that are not 16-byte aligned.
+#pragma unroll 1
+  for (; g < groups && ok; ++g) {
+    const uint32_t off = g * WS_GROUP_BYTES + lane * 16u;
+    uint32_t r[4] = {0, 0, 0, 0};
+    if (g < dec_groups) {
+      stage();
+      if (!ok) break;
+      const int first = (int)(g * WS_GROUP_WORDS + lane * WS_WORDS_PER_LANE);
+      const int valid = max(0, min(8, (int)W - first));
+      uint32_t ea0, eb0, ea1, eb1;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        ea0 = eb0 = ea1 = eb1 = 0;
+        if (2 * c < valid) WS_STEP_C(ea0, eb0);
+        if (2 * c + 1 < valid) WS_STEP_C(ea1, eb1);
+        r[c] = __byte_perm(__byte_perm(ea0, eb0, 0x0051), __byte_perm(ea1, eb1, 0x5100), 0x7610);
+        WS_RENORM_C();
+      }
+    }
+    uint32_t out[4] = {0, 0, 0, 0};
+    apply_chunk_bytes<U16, REVERSE>(dst + off, off, n, r, coded_bytes, bd.tail, out);
+    ck.add(out[0], out[1], out[2], out[3]);
   }
   if (!ok) {
     if (lane == 0) report(res, WS_DEVERR_TIMEOUT, block);
@@ -348,7 +456,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t block = tile.first_block + warp;
   const ws_block_desc bd = blocks[block];
   const uint8_t* src = payload + (bd.src - payload_offset);
-  uint8_t* ring = smem + kRingOffset + warp * WS_RING_BYTES;
+  uint8_t* ring = smem + kRingOffset + warp * kRingStride;
   switch (bd.kind) {
     case WS_KIND_RAW:
       raw_block(bd, block, src, lane, res);
@@ -367,6 +475,15 @@ __global__ void __launch_bounds__(kThreads, 2)
 }  // namespace
 
 size_t apply_smem_bytes() { return kSmemBytes; }
+
+cudaError_t prime_kernels() {
+  // Loads both kernel instantiations (lazy module loading) and sets their
+  // shared-memory limit, so the first apply of each direction pays nothing.
+  cudaError_t e = cudaFuncSetAttribute(ws_apply_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(ws_apply_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+  return e;
+}
 
 cudaError_t launch_apply(const ws_tile_desc* tiles, uint32_t tile_begin, uint32_t ntiles,
                          const ws_block_desc* blocks, const uint32_t* tables, const uint8_t* payload,
@@ -434,7 +551,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t block = tile.first_block + warp;
   const ws_block_desc bd = blocks[block];
   const uint8_t* src = payload + bd.src;
-  uint8_t* ring = smem + kRingOffset + warp * WS_RING_BYTES;
+  uint8_t* ring = smem + kRingOffset + warp * kRingStride;
   switch (bd.kind) {
     case WS_KIND_RAW:
       raw_block(bd, block, src, lane, res);

@@ -10,6 +10,9 @@ namespace ws {
 // Shared memory used by one CTA of the decode+apply kernel.
 size_t apply_smem_bytes();
 
+// Loads both kernel instantiations on the current device (call once before timing or capture).
+cudaError_t prime_kernels();
+
 // One launch over tiles [tile_begin, tile_begin + ntiles). `payload` is the
 // device address of arena byte `payload_offset` (a staging slot or the resident
 // copy); block descriptors hold arena offsets.

@@ -469,6 +469,7 @@ int ws_plan_upload(ws_plan* p, void* stream) {
     if (a) p->copy_done.push_back(a);
     if (b) p->compute_done.push_back(b);
   }
+  if (e == cudaSuccess) e = ws::prime_kernels();
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->start_event, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p->own_copy_stream, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
