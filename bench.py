@@ -232,8 +232,10 @@ class OracleSwitch:
         for i, name in enumerate(b):
             descs[i] = _lib.TensorDesc(a[name].data_ptr(), b[name].data_ptr(), b[name].numel() * b[name].element_size(),
                                        int(str(b[name].dtype) == "torch.bfloat16"), 0)
+        from warpshift_b200.delta import _DICT_SLACK_PCT
+
         opts = _lib.BuildOptions(policy=_lib.POLICIES[policy], threads=0, target_on_device=0, device=0,
-                                 batch_bytes=0, staging_slots=0, pin_arena=0)
+                                 batch_bytes=0, staging_slots=0, pin_arena=0, dict_slack_pct=_DICT_SLACK_PCT)
         self.plan = ctypes.c_void_p()
         _lib.check(lib.ws_plan_build(descs, len(a), ctypes.byref(opts), None, ctypes.byref(self.plan)))
         view, stats = _lib.PlanView(), _lib.PlanStats()

@@ -60,6 +60,10 @@ typedef struct ws_build_options {
   uint64_t batch_bytes;     /* bound on one H2D staging batch (0 = 16 MiB) */
   int32_t staging_slots;    /* device staging buffers (0 = 3) */
   int32_t pin_arena;        /* 1: arena in pinned host memory (needs CUDA); 0: malloc */
+  int32_t dict_slack_pct;   /* code a packet as one symbol per word (word dictionary) when its words
+                               take <= 255 values and the estimated size is at most this many percent
+                               above the byte-plane coding; negative: byte planes only */
+  int32_t reserved;
 } ws_build_options;
 
 typedef struct ws_plan_stats {

@@ -50,6 +50,8 @@ def lib() -> ctypes.CDLL:
         P, U32, U64, I32 = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int
         _lib.wso_decode_words.argtypes = [P, U32, U32, U32, P, P]
         _lib.wso_decode_words.restype = I32
+        _lib.wso_decode_dict_words.argtypes = [P, U32, U32, U32, P, P]
+        _lib.wso_decode_dict_words.restype = I32
         _lib.wso_block_hash.argtypes = [P, U32, U64]
         _lib.wso_block_hash.restype = U64
         _lib.wso_apply_plan.argtypes = [P, U64, P, U64, P, P, ctypes.c_int64, I32, I32, ctypes.POINTER(U64)]
@@ -63,7 +65,8 @@ def decode_words(payload: np.ndarray, block: np.void, table512: np.ndarray) -> t
     words = np.zeros(max(1, nbytes // 2), dtype="<u2")
     payload = np.ascontiguousarray(payload, dtype=np.uint8)
     table512 = np.ascontiguousarray(table512, dtype=np.uint32)
-    err = lib().wso_decode_words(
+    decode = lib().wso_decode_dict_words if int(block["kind"]) in (3, 4) else lib().wso_decode_words
+    err = decode(
         payload.ctypes.data, int(block["clen"]), int(block["nwords"]), nbytes, table512.ctypes.data, words.ctypes.data
     )
     return words[: nbytes // 2], err

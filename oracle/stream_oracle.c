@@ -21,6 +21,12 @@
  * Slot entry e of a 256-slot table: bias = e & 255, sym = (e >> 8) & 255,
  * freq = e >> 16; decode x -> freq * (x >> 8) + bias.
  * U16 blocks code y = rotr16(zigzag(d), 1); d = y ^ (y & 0x8000 ? 0x7FFF : 0).
+ *
+ * Word-dictionary blocks (kinds 3 and 4) decode one symbol per word with one
+ * shared table whose entry e gives word = e & 0xFFFF, bias = (e >> 16) & 255,
+ * freq = e >> 24. Lane l's state 0 decodes its words 0, 2, 4, 6 and state 1
+ * its words 1, 3, 5, 7 of each group; a check follows every second word of
+ * each state (after lane words 3 and 7), with the same read order.
  */
 #include <pthread.h>
 #include <stdint.h>
@@ -43,7 +49,7 @@ typedef struct {
   uint32_t first_block, nblocks, table, pad;
 } o_tile;
 
-enum { O_RAW = 0, O_ANS_XOR = 1, O_ANS_U16 = 2 };
+enum { O_RAW = 0, O_ANS_XOR = 1, O_ANS_U16 = 2, O_DICT_XOR = 3, O_DICT_U16 = 4 };
 enum { O_ERR_STATE = 1, O_ERR_LENGTH = 2, O_ERR_KIND = 8, O_ERR_BOUNDS = 16 };
 
 static inline uint16_t rd16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
@@ -94,6 +100,47 @@ int wso_decode_words(const uint8_t* payload, uint32_t clen, uint32_t nwords, uin
   return err;
 }
 
+/* Word-dictionary variant of wso_decode_words. */
+int wso_decode_dict_words(const uint8_t* payload, uint32_t clen, uint32_t nwords, uint32_t nbytes,
+                          const uint32_t* table256, uint16_t* words) {
+  const uint32_t W = nbytes / 2;
+  if (clen < 256 || 2ull * nwords > clen) return O_ERR_BOUNDS;
+  uint32_t x[2][32];
+  for (int p = 0; p < 2; ++p)
+    for (int l = 0; l < 32; ++l) x[p][l] = rd32(payload + 4 * (32 * p + l));
+  uint32_t pos = 128;
+  const uint32_t groups = (W + 255) / 256;
+  for (uint32_t g = 0; g < groups; ++g) {
+    for (uint32_t c = 0; c < 2; ++c) {
+      for (uint32_t l = 0; l < 32; ++l) {
+        for (uint32_t k = 0; k < 2; ++k) {
+          for (int p = 0; p < 2; ++p) {
+            const uint32_t i = 256 * g + 8 * l + 4 * c + 2 * k + (uint32_t)p;
+            if (i >= W) continue;
+            const uint32_t e = table256[x[p][l] & 255u];
+            const uint32_t freq = e >> 24, bias = (e >> 16) & 255u;
+            x[p][l] = freq * (x[p][l] >> 8) + bias;
+            words[i] = (uint16_t)(e & 0xFFFFu);
+          }
+        }
+      }
+      for (int p = 0; p < 2; ++p)
+        for (uint32_t l = 0; l < 32; ++l)
+          if (x[p][l] < O_L) {
+            const uint32_t w = (pos < nwords) ? rd16(payload + 2 * pos) : 0;
+            x[p][l] = (x[p][l] << 16) | w;
+            ++pos;
+          }
+    }
+  }
+  int err = 0;
+  for (int p = 0; p < 2; ++p)
+    for (int l = 0; l < 32; ++l)
+      if (x[p][l] != O_L) err |= O_ERR_STATE;
+  if (pos != nwords) err |= O_ERR_LENGTH;
+  return err;
+}
+
 static inline uint16_t o_unrotate(uint16_t y) { return (uint16_t)(y ^ ((y & 0x8000u) ? 0x7FFFu : 0u)); }
 
 /* Apply one block to dst (host memory). Returns 0 or O_ERR_*. */
@@ -105,12 +152,18 @@ int wso_apply_block(const o_block* b, const uint8_t* payload, const uint32_t* ta
     for (uint32_t i = 0; i < n; ++i) dst[i] ^= payload[i];
     return 0;
   }
-  if (b->kind != O_ANS_XOR && b->kind != O_ANS_U16) return O_ERR_KIND;
-  int err = wso_decode_words(payload, b->clen, b->nwords, n, table512, scratch_words);
+  int err;
+  if (b->kind == O_ANS_XOR || b->kind == O_ANS_U16)
+    err = wso_decode_words(payload, b->clen, b->nwords, n, table512, scratch_words);
+  else if (b->kind == O_DICT_XOR || b->kind == O_DICT_U16)
+    err = wso_decode_dict_words(payload, b->clen, b->nwords, n, table512, scratch_words);
+  else
+    return O_ERR_KIND;
+  const int xor_apply = b->kind == O_ANS_XOR || b->kind == O_DICT_XOR;
   const uint32_t W = n / 2;
   for (uint32_t i = 0; i < W; ++i) {
     uint16_t old = rd16(dst + 2 * i), nw;
-    if (b->kind == O_ANS_XOR) {
+    if (xor_apply) {
       nw = (uint16_t)(old ^ scratch_words[i]);
     } else {
       const uint16_t d = o_unrotate(scratch_words[i]);

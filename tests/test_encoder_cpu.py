@@ -20,18 +20,22 @@ from oracle import stream as ostream
 from tests.helpers import as_bytes, bf16_pair, edge_pair, host_plan, plan_arrays
 from warpshift_b200 import _lib
 
-KIND_RAW, KIND_XOR, KIND_U16 = 0, 1, 2
+KIND_RAW, KIND_XOR, KIND_U16, KIND_DICT_XOR, KIND_DICT_U16 = 0, 1, 2, 3, 4
 
 
 def clone(d):
     return {k: v.clone() for k, v in d.items()}
 
 
+CODINGS = {"planes": -1, "default": 6, "dictionary": 100}
+
+
+@pytest.mark.parametrize("coding", list(CODINGS))
 @pytest.mark.parametrize("policy", ["auto", "xor", "u16"])
-def test_host_plan_round_trips_through_the_oracle_decoder(policy: str) -> None:
+def test_host_plan_round_trips_through_the_oracle_decoder(policy: str, coding: str) -> None:
     a, b = edge_pair(seed=7)
     work = clone(b)
-    plan = host_plan(a, work, policy)
+    plan = host_plan(a, work, policy, dict_slack_pct=CODINGS[coding])
     try:
         blocks, tiles, tables, arena, stats = plan_arrays(plan)
         assert stats.runtime_bytes == sum(t.numel() * t.element_size() for t in b.values())
@@ -64,11 +68,12 @@ def test_mode_rule_follows_the_reference() -> None:
         _lib.load().ws_plan_destroy(plan)
 
 
+@pytest.mark.parametrize("coding", ["planes", "dictionary"])
 @pytest.mark.parametrize("policy", ["xor", "u16"])
-def test_coded_words_are_the_reference_residual(policy: str) -> None:
+def test_coded_words_are_the_reference_residual(policy: str, coding: str) -> None:
     a_t, b_t = bf16_pair(3 * 32768 + 1000, 0.01, 9)
     a, b = {"w": a_t}, {"w": b_t.clone()}
-    plan = host_plan(a, b, policy)
+    plan = host_plan(a, b, policy, dict_slack_pct=CODINGS[coding])
     try:
         blocks, tiles, tables, arena, stats = plan_arrays(plan)
         base, target = as_bytes(a_t), as_bytes(b_t)
@@ -86,9 +91,11 @@ def test_coded_words_are_the_reference_residual(policy: str) -> None:
             words, err = ostream.decode_words(payload, blk, table)
             assert err == 0
             w0 = (int(blk["dst"]) - b["w"].data_ptr()) // 2
-            ref = (rot if blk["kind"] == KIND_U16 else xor_words)[w0 : w0 + words.size]
+            ref = (rot if blk["kind"] in (KIND_U16, KIND_DICT_U16) else xor_words)[w0 : w0 + words.size]
             np.testing.assert_array_equal(words, ref, err_msg=f"block {i}")
-            assert blk["kind"] == (KIND_U16 if policy == "u16" else KIND_XOR)
+            expected = {("u16", "planes"): KIND_U16, ("xor", "planes"): KIND_XOR,
+                        ("u16", "dictionary"): KIND_DICT_U16, ("xor", "dictionary"): KIND_DICT_XOR}
+            assert blk["kind"] == expected[(policy, coding)]
     finally:
         _lib.load().ws_plan_destroy(plan)
 
@@ -157,3 +164,22 @@ def test_high_entropy_blocks_fall_back_to_raw_and_stay_exact() -> None:
     assert ostream.apply_plan(blocks, tiles, tables, arena, 0, True, 2)[0] == 0
     assert torch.equal(work["u"], u)
     _lib.load().ws_plan_destroy(plan)
+
+
+def test_dictionary_needs_few_distinct_words_and_planes_cover_the_rest() -> None:
+    """Word dictionary only for 2..255 distinct residual words; otherwise byte planes."""
+    a_t, b_t = bf16_pair(40000, 0.01, 12)  # ~100 distinct XOR words
+    rng = np.random.default_rng(4)
+    u = torch.from_numpy(rng.integers(0, 65536, 40000, dtype=np.uint16).astype(np.int16)).view(torch.bfloat16)
+    v = u.view(torch.int16).clone()
+    v[::3] ^= torch.from_numpy(rng.integers(1, 65536, v[::3].numel(), dtype=np.uint16).astype(np.int16))  # thousands of words
+    cases = {"few": ({"w": a_t}, {"w": b_t.clone()}), "many": ({"w": u}, {"w": v.view(torch.bfloat16)})}
+    for name, (a, b) in cases.items():
+        plan = host_plan(a, b, "xor", dict_slack_pct=100)
+        blocks, *_ = plan_arrays(plan)
+        kinds = set(int(k) for k in blocks["kind"])
+        if name == "few":
+            assert kinds == {KIND_DICT_XOR}
+        else:
+            assert KIND_DICT_XOR not in kinds
+        _lib.load().ws_plan_destroy(plan)

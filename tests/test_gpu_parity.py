@@ -29,11 +29,15 @@ def assert_bytes_equal(gpu: dict[str, torch.Tensor], ref: dict[str, torch.Tensor
         np.testing.assert_array_equal(as_bytes(t), as_bytes(ref[name]), err_msg=name)
 
 
+CODINGS = {"planes": -1, "dictionary": 100}
+
+
+@pytest.mark.parametrize("coding", list(CODINGS))
 @pytest.mark.parametrize("policy", ["auto", "xor", "u16"])
-def test_edge_cases_round_trip_bit_exact(cuda_device, policy: str) -> None:
+def test_edge_cases_round_trip_bit_exact(cuda_device, policy: str, coding: str) -> None:
     a, b = edge_pair(seed=1)
     gpu = to_device(b, cuda_device)
-    delta = DeltaWeights(a, gpu, policy=policy)
+    delta = DeltaWeights(a, gpu, policy=policy, dict_slack_pct=CODINGS[coding])
     assert set(delta.stats) >= {
         "codec", "reversible", "chunk_bytes", "batch_bytes", "runtime_bytes", "skipped_bytes", "payload_bytes",
         "transferred_bytes", "pinned_bytes", "mode_counts", "batches", "gpu_scratch_bytes", "gpu_metadata_bytes",
@@ -46,12 +50,13 @@ def test_edge_cases_round_trip_bit_exact(cuda_device, policy: str) -> None:
         assert delta.last_apply["ok"] and delta.last_apply["checksum"] == delta.last_apply["expected"]
 
 
+@pytest.mark.parametrize("coding", list(CODINGS))
 @pytest.mark.parametrize("policy", ["xor", "u16"])
-def test_decoded_residual_matches_oracle(cuda_device, policy: str) -> None:
+def test_decoded_residual_matches_oracle(cuda_device, policy: str, coding: str) -> None:
     """Apply onto zeroed weights: the kernel then writes the residual itself."""
     a, b = edge_pair(seed=2, big=False)
     gpu = to_device(b, cuda_device)
-    delta = DeltaWeights(a, gpu, policy=policy)
+    delta = DeltaWeights(a, gpu, policy=policy, dict_slack_pct=CODINGS[coding])
     for t in gpu.values():
         t.zero_()
     with pytest.raises(RuntimeError, match="checksum"):
@@ -124,8 +129,8 @@ def test_misaligned_destinations(cuda_device) -> None:
         a[f"parameter:v{k}"], b[f"parameter:v{k}"], ref_b[f"parameter:v{k}"] = x, view, y
         start += off + n
     assert all(v.data_ptr() % 16 for v in b.values())
-    for policy in ("xor", "u16"):
-        delta = DeltaWeights(a, b, policy=policy)
+    for policy, slack in (("xor", -1), ("u16", -1), ("xor", 100), ("u16", 100)):
+        delta = DeltaWeights(a, b, policy=policy, dict_slack_pct=slack)
         delta.apply(reverse=True)
         assert_bytes_equal(b, a)
         delta.apply(reverse=False)

@@ -33,6 +33,8 @@ class BuildOptions(ctypes.Structure):
         ("batch_bytes", u64),
         ("staging_slots", i32),
         ("pin_arena", i32),
+        ("dict_slack_pct", i32),
+        ("reserved", i32),
     ]
 
 

@@ -277,7 +277,60 @@ __device__ __forceinline__ uint32_t check_fast(uint32_t& xa, uint32_t& xb, uint3
   return out;
 }
 
-template <bool U16, bool REVERSE>
+// Dictionary-block check in hand-written PTX: two decode steps in which state
+// A decodes the lane's even word and state B the following odd word (one
+// table, entry = word | bias << 16 | freq << 24), then one renormalisation
+// check. out0/out1 receive words (2s, 2s+1) of steps s = 0, 1 as lo | hi << 16.
+__device__ __forceinline__ void check_dict(uint32_t& xa, uint32_t& xb, uint32_t& rp, uint32_t tb, uint32_t ltm,
+                                           uint32_t& out0, uint32_t& out1) {
+  asm volatile(
+      "{\n"
+      " .reg .u32 sa, sb, aa, ab, ea, eb, qa, qb, fa, fb, ba, bb, va, vb, ca, cb, oa, ob, t, ada, adb, wa, wb;\n"
+      " .reg .pred pa, pb;\n"
+      " and.b32 sa, %0, 255;\n and.b32 sb, %1, 255;\n"
+      " mad.lo.u32 aa, sa, 128, %5;\n mad.lo.u32 ab, sb, 128, %5;\n"
+      " ld.shared.u32 ea, [aa];\n ld.shared.u32 eb, [ab];\n"
+      " shr.u32 qa, %0, 8;\n shr.u32 qb, %1, 8;\n"
+      " shr.u32 fa, ea, 24;\n shr.u32 fb, eb, 24;\n"
+      " prmt.b32 ba, ea, 0, 0x4442;\n prmt.b32 bb, eb, 0, 0x4442;\n"
+      " mad.lo.u32 %0, fa, qa, ba;\n mad.lo.u32 %1, fb, qb, bb;\n"
+      " prmt.b32 %2, ea, eb, 0x5410;\n"
+      " and.b32 sa, %0, 255;\n and.b32 sb, %1, 255;\n"
+      " mad.lo.u32 aa, sa, 128, %5;\n mad.lo.u32 ab, sb, 128, %5;\n"
+      " ld.shared.u32 ea, [aa];\n ld.shared.u32 eb, [ab];\n"
+      " shr.u32 qa, %0, 8;\n shr.u32 qb, %1, 8;\n"
+      " shr.u32 fa, ea, 24;\n shr.u32 fb, eb, 24;\n"
+      " prmt.b32 ba, ea, 0, 0x4442;\n prmt.b32 bb, eb, 0, 0x4442;\n"
+      " mad.lo.u32 %0, fa, qa, ba;\n mad.lo.u32 %1, fb, qb, bb;\n"
+      " prmt.b32 %3, ea, eb, 0x5410;\n"
+      " setp.lt.u32 pa, %0, 65536;\n setp.lt.u32 pb, %1, 65536;\n"
+      " vote.sync.ballot.b32 va, pa, 0xffffffff;\n vote.sync.ballot.b32 vb, pb, 0xffffffff;\n"
+      " popc.b32 ca, va;\n popc.b32 cb, vb;\n"
+      " and.b32 t, va, %6;\n popc.b32 oa, t;\n"
+      " and.b32 t, vb, %6;\n popc.b32 ob, t;\n add.u32 ob, ob, ca;\n"
+      " mad.lo.u32 ada, oa, 2, %4;\n mad.lo.u32 adb, ob, 2, %4;\n"
+      " @pa ld.shared.u16 wa, [ada];\n @pb ld.shared.u16 wb, [adb];\n"
+      " @pa prmt.b32 %0, wa, %0, 0x5410;\n @pb prmt.b32 %1, wb, %1, 0x5410;\n"
+      " add.u32 t, ca, cb;\n mad.lo.u32 %4, t, 2, %4;\n"
+      "}\n"
+      : "+r"(xa), "+r"(xb), "=r"(out0), "=r"(out1), "+r"(rp)
+      : "r"(tb), "r"(ltm));
+}
+
+// Generic-path dictionary step: state A decodes word j, state B word j + 1.
+#define WS_DICT_STEP_C(ea, eb, va, vb)                                  \
+  {                                                                     \
+    if (va) {                                                           \
+      ea = lds32(tb0 + ((xa & 255u) << 7));                             \
+      xa = (ea >> 24) * (xa >> 8) + ((ea >> 16) & 255u);                \
+    }                                                                   \
+    if (vb) {                                                           \
+      eb = lds32(tb0 + ((xb & 255u) << 7));                             \
+      xb = (eb >> 24) * (xb >> 8) + ((eb >> 16) & 255u);                \
+    }                                                                   \
+  }
+
+template <bool U16, bool REVERSE, bool DICT>
 __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t* __restrict__ src,
                           const uint32_t* __restrict__ tbl0, const uint32_t* __restrict__ tbl1, uint8_t* ring,
                           uint32_t bar_base, uint32_t lane, ws_device_result* res) {
@@ -359,10 +412,16 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
       const uint4 old = *p;
       uint32_t rp = ring_s + (pos & (kRingHalfwords - 1)) * 2u;
       const uint32_t rp0 = rp;
-      const uint32_t r0 = check_fast(xa, xb, rp, tb0, tb1, ltm);
-      const uint32_t r1 = check_fast(xa, xb, rp, tb0, tb1, ltm);
-      const uint32_t r2 = check_fast(xa, xb, rp, tb0, tb1, ltm);
-      const uint32_t r3 = check_fast(xa, xb, rp, tb0, tb1, ltm);
+      uint32_t r0, r1, r2, r3;
+      if (DICT) {
+        check_dict(xa, xb, rp, tb0, ltm, r0, r1);
+        check_dict(xa, xb, rp, tb0, ltm, r2, r3);
+      } else {
+        r0 = check_fast(xa, xb, rp, tb0, tb1, ltm);
+        r1 = check_fast(xa, xb, rp, tb0, tb1, ltm);
+        r2 = check_fast(xa, xb, rp, tb0, tb1, ltm);
+        r3 = check_fast(xa, xb, rp, tb0, tb1, ltm);
+      }
       pos += (rp - rp0) >> 1;
       uint4 v;
       if (U16) {
@@ -393,13 +452,27 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
       const int first = (int)(g * WS_GROUP_WORDS + lane * WS_WORDS_PER_LANE);
       const int valid = max(0, min(8, (int)W - first));
       uint32_t ea0, eb0, ea1, eb1;
+      if (DICT) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        ea0 = eb0 = ea1 = eb1 = 0;
-        if (2 * c < valid) WS_STEP_C(ea0, eb0);
-        if (2 * c + 1 < valid) WS_STEP_C(ea1, eb1);
-        r[c] = __byte_perm(__byte_perm(ea0, eb0, 0x0051), __byte_perm(ea1, eb1, 0x5100), 0x7610);
-        WS_RENORM_C();
+        for (int c = 0; c < 2; ++c) {
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const int j = 4 * c + 2 * k;
+            ea0 = eb0 = 0;
+            WS_DICT_STEP_C(ea0, eb0, j < valid, j + 1 < valid);
+            r[2 * c + k] = __byte_perm(ea0, eb0, 0x5410);
+          }
+          WS_RENORM_C();
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          ea0 = eb0 = ea1 = eb1 = 0;
+          if (2 * c < valid) WS_STEP_C(ea0, eb0);
+          if (2 * c + 1 < valid) WS_STEP_C(ea1, eb1);
+          r[c] = __byte_perm(__byte_perm(ea0, eb0, 0x0051), __byte_perm(ea1, eb1, 0x5100), 0x7610);
+          WS_RENORM_C();
+        }
       }
     }
     uint32_t out[4] = {0, 0, 0, 0};
@@ -462,10 +535,16 @@ __global__ void __launch_bounds__(kThreads, 2)
       raw_block(bd, block, src, lane, res);
       break;
     case WS_KIND_ANS_XOR:
-      ans_block<false, REVERSE>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
+      ans_block<false, REVERSE, false>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
       break;
     case WS_KIND_ANS_U16:
-      ans_block<true, REVERSE>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
+      ans_block<true, REVERSE, false>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
+      break;
+    case WS_KIND_DICT_XOR:
+      ans_block<false, REVERSE, true>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
+      break;
+    case WS_KIND_DICT_U16:
+      ans_block<true, REVERSE, true>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
       break;
     default:
       if (lane == 0) report(res, WS_DEVERR_KIND, block);
@@ -557,10 +636,16 @@ __global__ void __launch_bounds__(kThreads, 2)
       raw_block(bd, block, src, lane, res);
       break;
     case WS_KIND_ANS_XOR:
-      ans_block<false, REVERSE>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
+      ans_block<false, REVERSE, false>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
       break;
     case WS_KIND_ANS_U16:
-      ans_block<true, REVERSE>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
+      ans_block<true, REVERSE, false>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
+      break;
+    case WS_KIND_DICT_XOR:
+      ans_block<false, REVERSE, true>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
+      break;
+    case WS_KIND_DICT_U16:
+      ans_block<true, REVERSE, true>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
       break;
     default:
       if (lane == 0) report(res, WS_DEVERR_KIND, block);

@@ -42,42 +42,60 @@ void tables_from_counts(const uint64_t counts[2][256], PlaneTables* t, uint32_t 
   }
 }
 
-// Encode the two planes of one block (W words) in the decoder's interleaved
-// order. The decoder reads, at each check, one word for every lane whose plane-0
-// state fell below 2^16 (lane order), then one for every plane-1 state. Encoding
-// runs backwards, so words are pushed in the mirrored order and reversed at the end.
+// Symbol schedule of one block. Byte planes: state 0 decodes the low byte and
+// state 1 the high byte of each of the lane's 8 words per group, 2 words per
+// check (4 checks per group). Word dictionary: state 0 decodes the lane's words
+// 0, 2, 4, 6 and state 1 words 1, 3, 5, 7, one word per step, 2 steps per check
+// (2 checks per group). Symbol (check c, step k) of state s for lane l is the
+// one of word w = 256 g + 8 l + j; it is absent when w >= W.
+struct Schedule {
+  bool dict;
+  uint32_t checks_per_group() const { return dict ? 2u : 4u; }
+  uint32_t word(uint32_t g, uint32_t l, uint32_t c, uint32_t k, uint32_t s) const {
+    const uint32_t j = dict ? (4u * c + 2u * k + s) : (2u * c + k);
+    return g * WS_GROUP_WORDS + l * WS_WORDS_PER_LANE + j;
+  }
+};
+
+// Encode one block in the decoder's interleaved order. At each check the
+// decoder reads one word for every lane whose state-0 value fell below 2^16
+// (lane order), then for every state-1 value. Encoding runs backwards, so
+// words are pushed in the mirrored order and reversed at the end.
 //
 // Renormalisation rule (proof sketch): with M = 2^8 and I = [2^16, 2^32), the
 // states x that encode the pair (a then b in decode order) into I form the
 // interval [fa*fb, 2^16*fa*fb); for a single symbol, [2^8*f, 2^24*f). So the
 // encoder emits one 16-bit word exactly when x >= 2^16*fa*fb (resp. 2^24*f).
-void encode_ans_block(const uint8_t* p0, const uint8_t* p1, uint32_t W, const PlaneTables& t,
-                      std::vector<uint8_t>* payload, uint32_t* nwords) {
+// sym[s][w] is state s's symbol for word w; freq/cdf[s] its table.
+void encode_ans_block(const Schedule& sc, const uint8_t* const sym[2], uint32_t W, const uint32_t* const freq[2],
+                      const uint32_t* const cdf[2], std::vector<uint8_t>* payload, uint32_t* nwords) {
   uint32_t st[2][WS_LANES];
   for (int p = 0; p < 2; ++p)
     for (uint32_t l = 0; l < WS_LANES; ++l) st[p][l] = WS_RANS_L;
   std::vector<uint16_t> rev;
   rev.reserve(W + 64);
   const uint32_t groups = (W + WS_GROUP_WORDS - 1) / WS_GROUP_WORDS;
-  const uint32_t checks = groups * 4;
-  for (uint32_t c = checks; c-- > 0;) {
-    const uint32_t g = c >> 2, jj = (c & 3u) * 2u;
+  const uint32_t cpg = sc.checks_per_group();
+  const uint32_t checks = groups * cpg;
+  for (uint32_t cc = checks; cc-- > 0;) {
+    const uint32_t g = cc / cpg, c = cc % cpg;
     for (int p = 1; p >= 0; --p) {
-      const uint8_t* sy = p ? p1 : p0;
-      const uint32_t* freq = t.freq[p];
-      const uint32_t* cdf = t.cdf[p];
+      const uint8_t* sy = sym[p];
+      const uint32_t* fq = freq[p];
+      const uint32_t* cd = cdf[p];
       for (int l = WS_LANES - 1; l >= 0; --l) {
-        const uint32_t ia = g * WS_GROUP_WORDS + (uint32_t)l * WS_WORDS_PER_LANE + jj;
-        if (ia >= W) continue;
-        const bool has_b = ia + 1 < W;
+        const uint32_t wa = sc.word(g, (uint32_t)l, c, 0, (uint32_t)p);
+        if (wa >= W) continue;
+        const uint32_t wb = sc.word(g, (uint32_t)l, c, 1, (uint32_t)p);
+        const bool has_b = wb < W;
         uint32_t x = st[p][l];
-        const uint32_t sa = sy[ia];
-        const uint32_t fa = freq[sa];
+        const uint32_t sa = sy[wa];
+        const uint32_t fa = fq[sa];
         uint64_t xmax;
         uint32_t sb = 0, fb = 0;
         if (has_b) {
-          sb = sy[ia + 1];
-          fb = freq[sb];
+          sb = sy[wb];
+          fb = fq[sb];
           xmax = ((uint64_t)fa * fb) << 16;
         } else {
           xmax = (uint64_t)fa << 24;
@@ -86,8 +104,8 @@ void encode_ans_block(const uint8_t* p0, const uint8_t* p1, uint32_t W, const Pl
           rev.push_back((uint16_t)(x & 0xFFFFu));
           x >>= 16;
         }
-        if (has_b) x = ((x / fb) << WS_PROB_BITS) + (x % fb) + cdf[sb];
-        x = ((x / fa) << WS_PROB_BITS) + (x % fa) + cdf[sa];
+        if (has_b) x = ((x / fb) << WS_PROB_BITS) + (x % fb) + cd[sb];
+        x = ((x / fa) << WS_PROB_BITS) + (x % fa) + cd[sa];
         st[p][l] = x;
       }
     }
@@ -130,31 +148,83 @@ struct Candidate {
   std::vector<EncodedBlock> blocks;
 };
 
+// Estimated payload bytes of a coding: ideal code length under the quantised
+// frequencies plus per-block header and padding.
+double estimate_bytes(const uint64_t* counts, const uint32_t* freq, int nsym, uint32_t nblocks) {
+  double bits = 0;
+  for (int s = 0; s < nsym; ++s)
+    if (counts[s]) bits += (double)counts[s] * std::log2((double)WS_PROB_SCALE / (double)freq[s]);
+  return bits / 8.0 + nblocks * (2.0 * WS_HEADER_HALFWORDS + 10.0);
+}
+
+template <bool U16>
+inline uint16_t residual_word(const uint8_t* base, const uint8_t* target, uint64_t w) {
+  if (U16) return u16_symbol_word(load_u16(base + 2 * w), load_u16(target + 2 * w));
+  return (uint16_t)(load_u16(base + 2 * w) ^ load_u16(target + 2 * w));
+}
+
+// Builds the packet's coding for one residual transform: the byte-plane coding,
+// or the word-dictionary coding when the packet's words take 2..255 distinct
+// values and its estimated size is within dict_slack_pct percent of the planes'.
 template <bool U16>
 void build_candidate(const uint8_t* base, const uint8_t* target, uint64_t n, const std::vector<uint8_t>& nonzero,
-                     Candidate* cand) {
+                     int dict_slack_pct, Candidate* cand) {
   const uint64_t W = n / 2;  // coded words; an odd last byte is carried raw in the block's tail field
   uint64_t counts[2][256];
   memset(counts, 0, sizeof(counts));
+  std::vector<uint32_t> word_counts(65536, 0);
   const uint32_t nblk = (uint32_t)((n + WS_BLOCK_BYTES - 1) / WS_BLOCK_BYTES);
+  uint32_t coded_blocks = 0;
   for (uint32_t k = 0; k < nblk; ++k) {
     if (!nonzero[k]) continue;
+    ++coded_blocks;
     const uint64_t w0 = (uint64_t)k * (WS_BLOCK_BYTES / 2);
     const uint64_t w1 = std::min<uint64_t>(W, w0 + WS_BLOCK_BYTES / 2);
     for (uint64_t w = w0; w < w1; ++w) {
-      uint16_t v;
-      if (U16)
-        v = u16_symbol_word(load_u16(base + 2 * w), load_u16(target + 2 * w));
-      else
-        v = (uint16_t)(load_u16(base + 2 * w) ^ load_u16(target + 2 * w));
+      const uint16_t v = residual_word<U16>(base, target, w);
       counts[0][v & 0xFF]++;
       counts[1][v >> 8]++;
+      word_counts[v]++;
     }
   }
   PlaneTables t;
-  tables_from_counts(counts, &t, cand->table);
-  cand->size = 1024;  // compact per-packet tables (2 x 256 frequencies of 9 bits, rounded)
-  std::vector<uint8_t> p0(WS_BLOCK_BYTES / 2), p1(WS_BLOCK_BYTES / 2);
+  uint32_t plane_entries[512];
+  tables_from_counts(counts, &t, plane_entries);
+  const double planes_est = estimate_bytes(counts[0], t.freq[0], 256, coded_blocks) +
+                            estimate_bytes(counts[1], t.freq[1], 256, 0);
+  // Word dictionary: symbols are indices of the distinct words in increasing order.
+  std::vector<uint16_t> words;
+  for (uint32_t v = 0; v < 65536; ++v)
+    if (word_counts[v]) words.push_back((uint16_t)v);
+  bool use_dict = false;
+  uint32_t dict_freq[256], dict_cdf[256], dict_entries[512];
+  std::vector<uint8_t> index_of;
+  if (dict_slack_pct >= 0 && words.size() >= 2 && words.size() <= 255) {
+    uint64_t dcounts[256];
+    memset(dcounts, 0, sizeof(dcounts));
+    for (size_t i = 0; i < words.size(); ++i) dcounts[i] = word_counts[words[i]];
+    quantize_frequencies(dcounts, dict_freq);
+    const double dict_est = estimate_bytes(dcounts, dict_freq, 256, coded_blocks);
+    if (dict_est <= planes_est * (1.0 + dict_slack_pct / 100.0)) {
+      use_dict = true;
+      uint32_t c = 0, slot = 0;
+      for (uint32_t i = 0; i < 256; ++i) {
+        dict_cdf[i] = c;
+        c += dict_freq[i];
+      }
+      memset(dict_entries, 0, sizeof(dict_entries));
+      for (size_t i = 0; i < words.size(); ++i)
+        for (uint32_t k = 0; k < dict_freq[i]; ++k, ++slot) dict_entries[slot] = WS_DICT_ENTRY(k, words[i], dict_freq[i]);
+      index_of.assign(65536, 0);
+      for (size_t i = 0; i < words.size(); ++i) index_of[words[i]] = (uint8_t)i;
+    }
+  }
+  memcpy(cand->table, use_dict ? dict_entries : plane_entries, sizeof(cand->table));
+  cand->size = 1024;  // compact per-packet tables (frequencies, and the dictionary words)
+  const Schedule sc{use_dict};
+  const uint32_t* freq[2] = {use_dict ? dict_freq : t.freq[0], use_dict ? dict_freq : t.freq[1]};
+  const uint32_t* cdf[2] = {use_dict ? dict_cdf : t.cdf[0], use_dict ? dict_cdf : t.cdf[1]};
+  std::vector<uint8_t> s0(WS_BLOCK_BYTES / 2), s1(WS_BLOCK_BYTES / 2);
   for (uint32_t k = 0; k < nblk; ++k) {
     if (!nonzero[k]) continue;
     EncodedBlock blk;
@@ -166,20 +236,21 @@ void build_candidate(const uint8_t* base, const uint8_t* target, uint64_t n, con
     const uint8_t* bb = base + blk.offset;
     const uint8_t* tb = target + blk.offset;
     for (uint32_t w = 0; w < wb; ++w) {
-      uint16_t v;
-      if (U16)
-        v = u16_symbol_word(load_u16(bb + 2 * w), load_u16(tb + 2 * w));
-      else
-        v = (uint16_t)(load_u16(bb + 2 * w) ^ load_u16(tb + 2 * w));
-      p0[w] = (uint8_t)(v & 0xFF);
-      p1[w] = (uint8_t)(v >> 8);
+      const uint16_t v = residual_word<U16>(bb, tb, w);
+      if (use_dict) {
+        s0[w] = s1[w] = index_of[v];
+      } else {
+        s0[w] = (uint8_t)(v & 0xFF);
+        s1[w] = (uint8_t)(v >> 8);
+      }
     }
     if (blk.nbytes & 1u) {
       blk.flags |= WS_FLAG_ODD_TAIL;
       blk.tail = (uint8_t)(bb[blk.nbytes - 1] ^ tb[blk.nbytes - 1]);
     }
-    encode_ans_block(p0.data(), p1.data(), wb, t, &blk.payload, &blk.nwords);
-    blk.kind = U16 ? WS_KIND_ANS_U16 : WS_KIND_ANS_XOR;
+    const uint8_t* sym[2] = {s0.data(), s1.data()};
+    encode_ans_block(sc, sym, wb, freq, cdf, &blk.payload, &blk.nwords);
+    blk.kind = use_dict ? (U16 ? WS_KIND_DICT_U16 : WS_KIND_DICT_XOR) : (U16 ? WS_KIND_ANS_U16 : WS_KIND_ANS_XOR);
     const uint32_t raw = round_up16(blk.nbytes);
     if (blk.payload.size() >= raw) {  // incompressible block: carry its XOR bytes raw
       blk.kind = WS_KIND_RAW;
@@ -290,7 +361,7 @@ uint64_t block_lane_sum(const uint8_t* bytes, uint32_t n) {
 }
 
 void encode_packet(const uint8_t* base, const uint8_t* target, uint64_t n, bool is_bf16, int policy,
-                   EncodedPacket* out) {
+                   int dict_slack_pct, EncodedPacket* out) {
   out->nbytes = n;
   out->blocks.clear();
   out->zero_block_bytes = 0;
@@ -316,7 +387,7 @@ void encode_packet(const uint8_t* base, const uint8_t* target, uint64_t n, bool 
   const bool try_u16 = big && is_bf16 && (n % 2 == 0) && policy != 1;
   if (try_xor) {
     Candidate c;
-    build_candidate<false>(base, target, n, nonzero, &c);
+    build_candidate<false>(base, target, n, nonzero, dict_slack_pct, &c);
     if (c.size < best) {  // delta.py:188-189: strictly smaller replaces raw
       best = c.size;
       mode = (n % 2 == 0) ? WS_MODE_XOR_GROUP2_ANS : WS_MODE_XOR_ANS;
@@ -325,7 +396,7 @@ void encode_packet(const uint8_t* base, const uint8_t* target, uint64_t n, bool 
   }
   if (try_u16) {
     Candidate c;
-    build_candidate<true>(base, target, n, nonzero, &c);
+    build_candidate<true>(base, target, n, nonzero, dict_slack_pct, &c);
     if (c.size < best) {  // delta.py:192-193: strictly smaller than the current best
       best = c.size;
       mode = WS_MODE_U16_ANS;

@@ -40,8 +40,10 @@ void build_slot_entries(const uint32_t freqs[256], uint32_t entries[256]);
 void u16_residual_reference(const uint8_t* base, const uint8_t* target, uint64_t nbytes, uint8_t* out);
 
 // Encode one packet (<= WS_PACKET_BYTES) following delta.py:176-194 with our codec.
+// dict_slack_pct: use the word-dictionary coding when its estimated size is at
+// most this many percent above the byte-plane coding (negative: never).
 void encode_packet(const uint8_t* base, const uint8_t* target, uint64_t nbytes, bool is_bf16, int policy,
-                   EncodedPacket* out);
+                   int dict_slack_pct, EncodedPacket* out);
 
 // Checksum lane sum of `n` bytes (one block) as defined in ws_format.h.
 uint64_t block_lane_sum(const uint8_t* bytes, uint32_t n);

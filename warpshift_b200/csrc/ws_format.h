@@ -21,6 +21,11 @@
 //   * states are checked for renormalisation after every second decode step;
 //     with 8-bit precision two symbols lower a state by at most 2^16, so one
 //     16-bit read per check restores it.
+//   * a packet is coded either as two byte planes (above) or, when its 16-bit
+//     residual words take at most 255 distinct values, as one symbol per word
+//     from a per-packet word dictionary: each slot entry then carries the
+//     16-bit word itself, and the lane's two states decode alternate words
+//     (state A words 0, 2, 4, 6 and state B words 1, 3, 5, 7 of the lane's 8).
 #pragma once
 #include <stdint.h>
 
@@ -44,7 +49,13 @@
 enum ws_mode { WS_MODE_XOR_RAW = 0, WS_MODE_XOR_GROUP2_ANS = 1, WS_MODE_XOR_ANS = 2, WS_MODE_U16_ANS = 3, WS_MODE_SKIP = 4 };
 
 // Block kinds (per 64 KiB block inside a packet). All-zero blocks are omitted.
-enum ws_kind { WS_KIND_RAW = 0, WS_KIND_ANS_XOR = 1, WS_KIND_ANS_U16 = 2 };
+enum ws_kind {
+  WS_KIND_RAW = 0,       // payload = raw XOR bytes
+  WS_KIND_ANS_XOR = 1,   // byte planes, XOR apply
+  WS_KIND_ANS_U16 = 2,   // byte planes, wrapping u16 apply
+  WS_KIND_DICT_XOR = 3,  // word dictionary, XOR apply
+  WS_KIND_DICT_U16 = 4   // word dictionary, wrapping u16 apply
+};
 #define WS_FLAG_ODD_TAIL 1u  // block's last byte (odd packet size) is not coded; its XOR value is `tail`
 
 // Device-side errors reported through ws_device_result.errors.
@@ -74,9 +85,12 @@ typedef struct ws_tile_desc {
 } ws_tile_desc;
 #define WS_NO_TABLE 0xFFFFFFFFu
 
-// Slot entry of a decode table: bits 0-7 bias = slot - cdf[sym], bits 8-15 sym,
-// bits 16-24 freq (1..256).
+// Slot entry of a byte-plane table: bits 0-7 bias = slot - cdf[sym], bits 8-15
+// sym, bits 16-24 freq (1..256). A packet table holds plane 0 then plane 1.
 #define WS_ENTRY(bias, sym, freq) ((uint32_t)(bias) | ((uint32_t)(sym) << 8) | ((uint32_t)(freq) << 16))
+// Slot entry of a word-dictionary table: bits 0-15 the residual word, bits
+// 16-23 bias, bits 24-31 freq (1..255). Only the first 256 entries are used.
+#define WS_DICT_ENTRY(bias, word, freq) ((uint32_t)(word) | ((uint32_t)(bias) << 16) | ((uint32_t)(freq) << 24))
 
 // Accumulators written by the kernel for one apply.
 typedef struct ws_device_result {

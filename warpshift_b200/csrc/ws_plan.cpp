@@ -164,7 +164,7 @@ int encode_all(const ws_tensor_desc* tensors, const std::vector<PacketRef>& pack
       const PacketRef& pr = packets[i];
       const ws_tensor_desc& t = tensors[pr.tensor];
       ws::encode_packet((const uint8_t*)t.base + pr.offset, (const uint8_t*)t.target + pr.offset, pr.nbytes,
-                        t.is_bf16 != 0, o.policy, &(*out)[i]);
+                        t.is_bf16 != 0, o.policy, o.dict_slack_pct, &(*out)[i]);
     });
     return WS_OK;
   }
@@ -203,7 +203,7 @@ int encode_all(const ws_tensor_desc* tensors, const std::vector<PacketRef>& pack
         worker_error = true;
       } else {
         ws::encode_packet((const uint8_t*)t.base + pr.offset, bufs[job.second], pr.nbytes, t.is_bf16 != 0,
-                          o.policy, &(*out)[job.first]);
+                          o.policy, o.dict_slack_pct, &(*out)[job.first]);
       }
       {
         std::lock_guard<std::mutex> lk(mu);

@@ -28,6 +28,10 @@ _CHUNK_BYTES = 16 * 1024**2  # delta.py:20, packet size
 _BATCH_BYTES = 64 * 1024**2  # delta.py:21, default bound of _batch_layout
 _BLOCK_BYTES = 65536  # rANS block: one warp decodes one block
 _STAGING_BATCH_BYTES = 16 * 1024**2  # H2D staging batch of this implementation
+# A packet whose 16-bit residual words take <= 255 values may be coded one
+# symbol per word (half the decode work of the two byte planes); it is chosen
+# when its estimated size is at most this many percent above the planes'.
+_DICT_SLACK_PCT = 6
 _MODES = {0: "XOR_RAW", 1: "XOR_GROUP2_ANS", 2: "XOR_ANS", 3: "U16_ANS"}  # delta.py:23
 
 
@@ -85,6 +89,7 @@ class DeltaWeights:
         threads: int = 0,
         batch_bytes: int = _STAGING_BATCH_BYTES,
         staging_slots: int = 3,
+        dict_slack_pct: int = _DICT_SLACK_PCT,
     ) -> None:
         started = time.perf_counter()
         if policy not in _lib.POLICIES:
@@ -113,6 +118,7 @@ class DeltaWeights:
             batch_bytes=batch_bytes,
             staging_slots=staging_slots,
             pin_arena=1,
+            dict_slack_pct=dict_slack_pct,
         )
         plan = ctypes.c_void_p()
         with torch.cuda.device(self.device):
@@ -141,6 +147,7 @@ class DeltaWeights:
             "prepare_seconds": time.perf_counter() - started,
             # Additions of this implementation.
             "policy": policy,
+            "dict_slack_pct": dict_slack_pct,
             "block_bytes": _BLOCK_BYTES,
             "touched_bytes": int(native.touched_bytes),
             "zero_block_bytes": int(native.zero_block_bytes),
