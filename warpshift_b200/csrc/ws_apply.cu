@@ -38,7 +38,8 @@ constexpr uint32_t kBarOffset = kRingOffset + kWarps * kRingStride;
 constexpr uint32_t kSmemBytes = kBarOffset + kWarps * 2 * 8;
 constexpr uint32_t kRingHalfwords = WS_RING_BYTES / 2;      // 1024
 constexpr uint32_t kHalfHalfwords = WS_RING_HALF_BYTES / 2; // 512
-constexpr uint32_t kWaitLimit = 1u << 20;                   // bounded spin on a staging barrier
+constexpr uint32_t kWaitLimit = 1u << 20;      // bounded spin on a staging barrier
+constexpr uint32_t kPrefetchGroups = 3;        // destination groups requested into L2 ahead of their load
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -50,6 +51,20 @@ __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
 __device__ __forceinline__ uint32_t lds16(uint32_t addr) {
   uint16_t v;
   asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+  return v;
+}
+
+// Asks the TMA unit to pull `bytes` of global memory into L2 (no registers, no
+// completion to wait for): hides DRAM latency of the destination loads.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// 16-byte global load issued exactly where it appears (volatile keeps it ahead
+// of the hand-written decode blocks, so it is not sunk to its first use).
+__device__ __forceinline__ uint4 ldg128_early(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
   return v;
 }
 
@@ -399,6 +414,13 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
   {
     uint32_t next_event = 0;
     uint4* p = reinterpret_cast<uint4*>(dst + lane * 16u);
+    // The destination vector of group g + 1 is loaded while group g decodes,
+    // and groups further ahead are pulled into L2 by the TMA unit, so the DRAM
+    // latency of the destination stream stays hidden at high bandwidth.
+    uint4 next_old = make_uint4(0, 0, 0, 0);
+    if (lane == 0)
+      for (uint32_t k = 1; k <= kPrefetchGroups && k < fast_groups; ++k) prefetch_l2(dst + k * WS_GROUP_BYTES, WS_GROUP_BYTES);
+    if (fast_groups > 0) next_old = ldg128_early(p);
 #pragma unroll 1
     for (; g < fast_groups; ++g, p += WS_GROUP_BYTES / 16) {
       if (pos >= next_event) {
@@ -409,7 +431,10 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
             (ready < issued && bd.nwords > kHalfHalfwords * ready) ? kHalfHalfwords * ready - 255u : 0xFFFFFFFFu;
         next_event = min(recycle, wait);
       }
-      const uint4 old = *p;
+      const uint4 old = next_old;
+      if (g + 1 < fast_groups) next_old = ldg128_early(p + WS_GROUP_BYTES / 16);
+      if (lane == 0 && g + 1 + kPrefetchGroups < fast_groups)
+        prefetch_l2(dst + (g + 1 + kPrefetchGroups) * WS_GROUP_BYTES, WS_GROUP_BYTES);
       uint32_t rp = ring_s + (pos & (kRingHalfwords - 1)) * 2u;
       const uint32_t rp0 = rp;
       uint32_t r0, r1, r2, r3;
