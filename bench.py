@@ -336,14 +336,21 @@ def run_ours(args) -> None:
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     spec, desc = workload_spec(args, world, rank)
-    cpu_base, gpu = generate_on_device(spec, device, args.scale)
-    sample = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sample = host_sample(spec, cpu_base, gpu, 1 << 30)
-    t0 = time.perf_counter()
-    delta = DeltaWeights(cpu_base, gpu, policy=args.policy, threads=args.threads)
-    prepare_s = time.perf_counter() - t0
-    del cpu_base
+    # Ranks generate and prepare one at a time: each holds its Teacher1 copy in
+    # host memory only during its own turn, so peak host memory is one model
+    # plus the compressed arenas, whatever the number of ranks on the node.
+    sample, delta, gpu, prepare_s = None, None, None, 0.0
+    for turn in range(world):
+        if turn == rank:
+            cpu_base, gpu = generate_on_device(spec, device, args.scale)
+            if rank == 0 and world == 1 and not args.no_cpu_baseline:
+                sample = host_sample(spec, cpu_base, gpu, 1 << 30)
+            t0 = time.perf_counter()
+            delta = DeltaWeights(cpu_base, gpu, policy=args.policy, threads=args.threads)
+            prepare_s = time.perf_counter() - t0
+            del cpu_base
+        if group is not None:
+            dist.barrier(group=group)
     stats = delta.stats
     native = delta.native_stats()
     W = stats["runtime_bytes"]
@@ -440,7 +447,7 @@ def run_ours(args) -> None:
     achieved = algo_bytes / (avg_step_ms * 1e-3) / 1e9
     pk = peaks()
     traffic = None
-    traffic_file = ROOT / "profiles" / "traffic.json"
+    traffic_file = ROOT / "profiles" / "ws_apply_kernel_dram_traffic.json"
     if traffic_file.exists():
         entry = json.loads(traffic_file.read_text()).get(f"{args.workload}/{args.policy}/{args.scale}")
         if entry:
