@@ -55,6 +55,9 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--threads", type=int, default=0, help="host encoder threads (0 = all)")
     p.add_argument("--layers", type=int, default=0, help="truncate the model to N layers (small profiling cases)")
     p.add_argument("--skip-e2e", action="store_true", help="time only the kernel-only switch (profiling cases)")
+    p.add_argument("--tp", type=int, default=0, help="tensor-parallel degree of the 70B shard (default: number of ranks)")
+    p.add_argument("--compare-full-copy", action="store_true",
+                   help="also time the pinned full-backup restore path (copy_ of every tensor from pinned host memory)")
     return p.parse_args()
 
 
@@ -152,7 +155,8 @@ def workload_spec(args, world: int, rank: int):
         shape = dataclasses.replace(shape, layers=min(args.layers, shape.layers))
         suffix = f", truncated to {shape.layers} layers"
     if args.workload == "llama3-70b":
-        return synth.model_spec(shape, tp=world, rank=rank), f"llama3-70b tp={world} rank shard{suffix}"
+        tp = args.tp or world
+        return synth.model_spec(shape, tp=tp, rank=rank % tp), f"llama3-70b tp={tp} rank-{rank % tp} shard{suffix}"
     if args.workload == "mixtral-8x7b":
         return synth.model_spec(shape, tp=8, rank=rank % 8), f"mixtral-8x7b tp=8 shard per rank{suffix}"
     return synth.model_spec(shape), f"{args.workload} tp=1 per rank{suffix}"
@@ -437,6 +441,39 @@ def run_ours(args) -> None:
             e2e_ms = e_begin.elapsed_time(e_end)
     clocks = sampler.summary()
 
+    full_copy = None
+    if args.compare_full_copy:
+        # weights.py:65-70 pinned backup, then 77-82 restore: copy_ every tensor, sync.
+        backup = {}
+        for name, t in gpu.items():
+            backup[name] = torch.empty_like(t, device="cpu", pin_memory=True)
+            backup[name].copy_(t)
+        torch.cuda.synchronize(device)
+        caller = torch.cuda.current_stream(device)
+        for _ in range(max(1, args.warmup)):
+            for name, t in gpu.items():
+                t.copy_(backup[name], non_blocking=True)
+            torch.cuda.synchronize(device)
+        barrier()
+        f_begin, f_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f_begin.record(caller)
+        for _ in range(args.steps):
+            for name, t in gpu.items():
+                t.copy_(backup[name], non_blocking=True)
+            torch.cuda.synchronize(device)
+        f_end.record(caller)
+        torch.cuda.synchronize(device)
+        barrier()
+        f_ms = max_over_ranks(f_begin.elapsed_time(f_end))
+        full_copy = {
+            "value": round(sum_over_ranks(W) * args.steps / (f_ms * 1e-3) / 1e9, 2),
+            "unit": UNIT,
+            "ms_per_step": round(f_ms / args.steps, 3),
+            "h2d_bytes_per_step": W,
+            "path": "pinned full-backup restore (weights.py:65-82): torch copy_ per tensor from pinned host memory",
+        }
+        del backup
+
     kernel_ms_max = max_over_ranks(kernel_ms)
     e2e_ms_max = max_over_ranks(e2e_ms) if e2e_ms is not None else None
     W_total = sum_over_ranks(W)
@@ -514,6 +551,7 @@ def run_ours(args) -> None:
             "peak_source": pk["source"] + " (MEASURED_PEAKS.json hbm_gbs, burst copy)",
             "kernel": "ws_apply_kernel (fused rANS decode + in-place apply)",
         },
+        "full_copy": full_copy,
         "gpu_launches": launches_k + launches_e,
         "clocks": clocks,
     }
