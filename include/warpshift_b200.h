@@ -63,7 +63,8 @@ typedef struct ws_build_options {
   int32_t dict_slack_pct;   /* code a packet as one symbol per word (word dictionary) when its words
                                take <= 255 values and the estimated size is at most this many percent
                                above the byte-plane coding; negative: byte planes only */
-  int32_t reserved;
+  int32_t encode_on_device; /* 1 (with target_on_device): compute statistics and encode on the GPU,
+                               copying only A host->device; 0: copy B device->host, encode on host threads */
 } ws_build_options;
 
 typedef struct ws_plan_stats {

@@ -1,0 +1,79 @@
+"""GPU encoder (prepare on the device) against the host encoder: identical plans.
+
+Both encoders read the same A (host) and B (device) bytes; the GPU path copies
+only A to the device and computes statistics, tables' inputs and the rANS
+streams there. Their plans must match byte for byte: arena, block and tile
+descriptors, tables, expected checksums and mode counts.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from tests.helpers import bf16_pair, edge_pair, plan_arrays
+from warpshift_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+
+def build(a, b_dev, policy, slack, on_device):
+    lib = _lib.load()
+    descs = (_lib.TensorDesc * len(a))()
+    for i, name in enumerate(b_dev):
+        t = b_dev[name]
+        descs[i] = _lib.TensorDesc(a[name].data_ptr(), t.data_ptr(), t.numel() * t.element_size(),
+                                   int(t.dtype == torch.bfloat16), 0)
+    opts = _lib.BuildOptions(policy=_lib.POLICIES[policy], threads=4, target_on_device=1, device=0, batch_bytes=0,
+                             staging_slots=0, pin_arena=0, dict_slack_pct=slack, encode_on_device=int(on_device))
+    plan = ctypes.c_void_p()
+    stream = torch.cuda.current_stream().cuda_stream
+    _lib.check(lib.ws_plan_build(descs, len(a), ctypes.byref(opts), stream, ctypes.byref(plan)))
+    return plan
+
+
+def assert_same_plan(p_gpu, p_host) -> None:
+    bg, tg, tabg, ag, sg = plan_arrays(p_gpu)
+    bh, th, tabh, ah, sh = plan_arrays(p_host)
+    assert list(sg.mode_counts) == list(sh.mode_counts)
+    assert (sg.blocks, sg.tiles, sg.arena_bytes, sg.payload_bytes, sg.skipped_bytes, sg.zero_block_bytes) == (
+        sh.blocks, sh.tiles, sh.arena_bytes, sh.payload_bytes, sh.skipped_bytes, sh.zero_block_bytes)
+    assert list(sg.expected_checksum) == list(sh.expected_checksum)
+    np.testing.assert_array_equal(bg.view(np.uint8), bh.view(np.uint8))
+    np.testing.assert_array_equal(tg.view(np.uint8), th.view(np.uint8))
+    np.testing.assert_array_equal(tabg, tabh)
+    np.testing.assert_array_equal(ag, ah)
+
+
+@pytest.mark.parametrize("slack", [-1, 6, 100])
+@pytest.mark.parametrize("policy", ["auto", "xor", "u16"])
+def test_gpu_encoder_matches_host_encoder(cuda_device, policy: str, slack: int) -> None:
+    a, b = edge_pair(seed=13)
+    b_dev = {k: v.to(cuda_device) for k, v in b.items()}
+    lib = _lib.load()
+    p_gpu = build(a, b_dev, policy, slack, True)
+    p_host = build(a, b_dev, policy, slack, False)
+    try:
+        assert_same_plan(p_gpu, p_host)
+    finally:
+        lib.ws_plan_destroy(p_gpu)
+        lib.ws_plan_destroy(p_host)
+
+
+def test_gpu_encoder_matches_on_unaligned_views_and_many_packets(cuda_device) -> None:
+    x, y = bf16_pair((40 << 20) // 2 + 333, 0.01, 21)  # three packets, odd tail group
+    storage = torch.zeros(x.numel() + 8, dtype=torch.bfloat16, device=cuda_device)
+    view = storage[3 : 3 + x.numel()]
+    view.copy_(y)
+    lib = _lib.load()
+    for policy in ("auto", "xor"):
+        p_gpu = build({"w": x}, {"w": view}, policy, 6, True)
+        p_host = build({"w": x}, {"w": view}, policy, 6, False)
+        try:
+            assert_same_plan(p_gpu, p_host)
+        finally:
+            lib.ws_plan_destroy(p_gpu)
+            lib.ws_plan_destroy(p_host)

@@ -34,7 +34,7 @@ class BuildOptions(ctypes.Structure):
         ("staging_slots", i32),
         ("pin_arena", i32),
         ("dict_slack_pct", i32),
-        ("reserved", i32),
+        ("encode_on_device", i32),
     ]
 
 

@@ -187,43 +187,27 @@ void build_candidate(const uint8_t* base, const uint8_t* target, uint64_t n, con
       word_counts[v]++;
     }
   }
-  PlaneTables t;
-  uint32_t plane_entries[512];
-  tables_from_counts(counts, &t, plane_entries);
-  const double planes_est = estimate_bytes(counts[0], t.freq[0], 256, coded_blocks) +
-                            estimate_bytes(counts[1], t.freq[1], 256, 0);
-  // Word dictionary: symbols are indices of the distinct words in increasing order.
+  // Word dictionary candidates: the distinct words in increasing order.
   std::vector<uint16_t> words;
+  std::vector<uint64_t> wcounts;
   for (uint32_t v = 0; v < 65536; ++v)
-    if (word_counts[v]) words.push_back((uint16_t)v);
-  bool use_dict = false;
-  uint32_t dict_freq[256], dict_cdf[256], dict_entries[512];
-  std::vector<uint8_t> index_of;
-  if (dict_slack_pct >= 0 && words.size() >= 2 && words.size() <= 255) {
-    uint64_t dcounts[256];
-    memset(dcounts, 0, sizeof(dcounts));
-    for (size_t i = 0; i < words.size(); ++i) dcounts[i] = word_counts[words[i]];
-    quantize_frequencies(dcounts, dict_freq);
-    const double dict_est = estimate_bytes(dcounts, dict_freq, 256, coded_blocks);
-    if (dict_est <= planes_est * (1.0 + dict_slack_pct / 100.0)) {
-      use_dict = true;
-      uint32_t c = 0, slot = 0;
-      for (uint32_t i = 0; i < 256; ++i) {
-        dict_cdf[i] = c;
-        c += dict_freq[i];
-      }
-      memset(dict_entries, 0, sizeof(dict_entries));
-      for (size_t i = 0; i < words.size(); ++i)
-        for (uint32_t k = 0; k < dict_freq[i]; ++k, ++slot) dict_entries[slot] = WS_DICT_ENTRY(k, words[i], dict_freq[i]);
-      index_of.assign(65536, 0);
-      for (size_t i = 0; i < words.size(); ++i) index_of[words[i]] = (uint8_t)i;
+    if (word_counts[v]) {
+      words.push_back((uint16_t)v);
+      wcounts.push_back(word_counts[v]);
     }
+  CodingTables ct;
+  choose_coding(counts, words, wcounts, words.size() > 255, coded_blocks, dict_slack_pct, &ct);
+  const bool use_dict = ct.dict;
+  std::vector<uint8_t> index_of;
+  if (use_dict) {
+    index_of.assign(65536, 0);
+    for (size_t i = 0; i < ct.words.size(); ++i) index_of[ct.words[i]] = (uint8_t)i;
   }
-  memcpy(cand->table, use_dict ? dict_entries : plane_entries, sizeof(cand->table));
+  memcpy(cand->table, ct.entries, sizeof(cand->table));
   cand->size = 1024;  // compact per-packet tables (frequencies, and the dictionary words)
   const Schedule sc{use_dict};
-  const uint32_t* freq[2] = {use_dict ? dict_freq : t.freq[0], use_dict ? dict_freq : t.freq[1]};
-  const uint32_t* cdf[2] = {use_dict ? dict_cdf : t.cdf[0], use_dict ? dict_cdf : t.cdf[1]};
+  const uint32_t* freq[2] = {ct.freq[0], ct.freq[1]};
+  const uint32_t* cdf[2] = {ct.cdf[0], ct.cdf[1]};
   std::vector<uint8_t> s0(WS_BLOCK_BYTES / 2), s1(WS_BLOCK_BYTES / 2);
   for (uint32_t k = 0; k < nblk; ++k) {
     if (!nonzero[k]) continue;
@@ -328,6 +312,43 @@ void build_slot_entries(const uint32_t freqs[256], uint32_t entries[256]) {
   for (uint32_t s = 0; s < 256; ++s)
     for (uint32_t k = 0; k < freqs[s]; ++k, ++slot) entries[slot] = WS_ENTRY(k, s, freqs[s]);
   for (; slot < 256; ++slot) entries[slot] = 0;  // only reachable for an empty table
+}
+
+void choose_coding(const uint64_t counts[2][256], const std::vector<uint16_t>& words,
+                   const std::vector<uint64_t>& word_counts, bool many_words, uint32_t coded_blocks, int dict_slack_pct,
+                   CodingTables* out) {
+  PlaneTables t;
+  uint32_t plane_entries[512];
+  tables_from_counts(counts, &t, plane_entries);
+  const double planes_est = estimate_bytes(counts[0], t.freq[0], 256, coded_blocks) +
+                            estimate_bytes(counts[1], t.freq[1], 256, 0);
+  out->dict = false;
+  out->words.clear();
+  if (dict_slack_pct >= 0 && !many_words && words.size() >= 2 && words.size() <= 255) {
+    uint64_t dcounts[256];
+    uint32_t dict_freq[256];
+    memset(dcounts, 0, sizeof(dcounts));
+    for (size_t i = 0; i < words.size(); ++i) dcounts[i] = word_counts[i];
+    quantize_frequencies(dcounts, dict_freq);
+    const double dict_est = estimate_bytes(dcounts, dict_freq, 256, coded_blocks);
+    if (dict_est <= planes_est * (1.0 + dict_slack_pct / 100.0)) {
+      out->dict = true;
+      out->words = words;
+      uint32_t c = 0, slot = 0;
+      for (uint32_t i = 0; i < 256; ++i) {
+        out->freq[0][i] = out->freq[1][i] = dict_freq[i];
+        out->cdf[0][i] = out->cdf[1][i] = c;
+        c += dict_freq[i];
+      }
+      memset(out->entries, 0, sizeof(out->entries));
+      for (size_t i = 0; i < words.size(); ++i)
+        for (uint32_t k = 0; k < dict_freq[i]; ++k, ++slot) out->entries[slot] = WS_DICT_ENTRY(k, words[i], dict_freq[i]);
+      return;
+    }
+  }
+  memcpy(out->entries, plane_entries, sizeof(out->entries));
+  memcpy(out->freq, t.freq, sizeof(out->freq));
+  memcpy(out->cdf, t.cdf, sizeof(out->cdf));
 }
 
 void u16_residual_reference(const uint8_t* base, const uint8_t* target, uint64_t nbytes, uint8_t* out) {

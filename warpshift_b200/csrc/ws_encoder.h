@@ -29,6 +29,23 @@ struct EncodedPacket {
   std::vector<EncodedBlock> blocks;  // non-zero blocks in order
 };
 
+// Tables of one packet coding: byte planes (two tables) or word dictionary
+// (one table for both states, whose symbols index `words`).
+struct CodingTables {
+  bool dict = false;
+  uint32_t entries[512];          // slot entries as the kernel reads them
+  uint32_t freq[2][256], cdf[2][256];
+  std::vector<uint16_t> words;    // dictionary: word of each symbol, increasing
+};
+
+// Builds the byte-plane tables from `counts` (plane histograms over the coded
+// words) and switches to the word dictionary when the packet has 2..255
+// distinct words (`words` increasing, `word_counts` aligned; many_words = more
+// than 255) and its estimated size is within dict_slack_pct % of the planes'.
+void choose_coding(const uint64_t counts[2][256], const std::vector<uint16_t>& words,
+                   const std::vector<uint64_t>& word_counts, bool many_words, uint32_t coded_blocks, int dict_slack_pct,
+                   CodingTables* out);
+
 // Quantise symbol counts to frequencies summing to WS_PROB_SCALE; every symbol
 // with a non-zero count gets frequency >= 1. Greedy fix-up minimising code length.
 void quantize_frequencies(const uint64_t counts[256], uint32_t freqs[256]);

@@ -1,0 +1,665 @@
+// GPU encoder for prepare (replaces the host D2H + encode of delta.py:196-216,
+// 164-174 when the target weights are resident on the device).
+//
+// Per batch of packets:
+//   1. the base (A) bytes are copied host -> device;
+//   2. stats_kernel: per 64 KiB block, zero detection, byte-plane histograms and
+//      distinct-word tables of both residual transforms, checksum lane sums of
+//      A and B, odd tail byte;
+//   3. the host builds each packet's tables with the same code as the host
+//      encoder (choose_coding), so the output is byte-identical;
+//   4. encode_kernel: one warp per block and candidate coding, the exact mirror
+//      of the decoder (checks in reverse, ballot/popc word placement, division
+//      by reciprocal multiplication with one correction);
+//   5. the host applies the reference's mode rule and the raw fallback;
+//      compact_kernel packs the chosen payloads, which are copied back.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "ws_encoder.h"
+#include "ws_format.h"
+#include "ws_gpu_encoder.h"
+
+namespace ws {
+
+namespace {
+
+constexpr uint32_t kStatsThreads = 256;
+constexpr uint32_t kLocalSlots = 512;     // per-CTA distinct-word table
+constexpr uint32_t kPacketSlots = 1024;   // per-packet distinct-word table
+constexpr uint32_t kEncWarps = 8;         // blocks per encode CTA
+constexpr uint32_t kOutHalfwords = WS_HEADER_HALFWORDS + 32768u;  // header + worst-case stream
+constexpr uint32_t kMaxDistinct = 255;
+
+struct PacketStats {  // device, one per packet of the batch
+  uint32_t plane[2][2][256];  // [transform xor/u16][plane][symbol]
+  uint32_t key[2][kPacketSlots];  // word + 1, 0 = empty
+  uint32_t cnt[2][kPacketSlots];
+  uint32_t distinct[2];
+  uint32_t many[2];
+};
+
+struct BlockStats {  // device, one per block of the batch
+  uint32_t nonzero;
+  uint32_t tail;
+  unsigned long long lane_sum[2];  // [0] target (B) bytes, [1] base (A) bytes
+};
+
+struct BlockJob {  // one 64 KiB block of the batch
+  const uint8_t* base;    // device copy of A
+  const uint8_t* target;  // resident B
+  uint32_t nbytes;
+  uint32_t packet;        // packet index within the batch
+};
+
+struct EncodeJob {  // one block coded with one candidate
+  uint32_t block;     // index into the batch's BlockJob array
+  uint32_t table;     // index into the batch's encode tables
+  uint32_t dict;      // 1: word dictionary, 0: byte planes
+  uint32_t u16;       // 1: U16 residual words, 0: XOR words
+};
+
+struct EncTable {  // per candidate coding: per state, per symbol
+  uint32_t fc[2][256];   // freq | cdf << 16
+  uint32_t rcp[2][256];  // floor(2^32 / freq) (0xFFFFFFFF for freq 1)
+};
+
+struct CompactJob {
+  uint32_t block;      // BlockJob index
+  uint32_t encode;     // EncodeJob index (source of an ANS payload), or ~0u for raw
+  uint32_t nwords;     // ANS halfwords incl. header
+  uint32_t pad;
+  uint64_t dst;        // byte offset in the output buffer
+};
+
+__device__ __forceinline__ uint16_t u16_word(uint16_t b, uint16_t t) {
+  const int32_t d = (int32_t)(int16_t)(uint16_t)(t - b);
+  const uint32_t z = ((uint32_t)(d * 2) ^ (uint32_t)(d >> 15)) & 0xFFFFu;
+  return (uint16_t)((z >> 1) | ((z & 1u) << 15));
+}
+
+__device__ __forceinline__ uint32_t word_hash(uint32_t w, uint32_t bits) { return (w * 0x9E3779B1u) >> (32 - bits); }
+
+// Insert one occurrence of word w into an open-addressing table; returns false
+// when the table cannot take another distinct word.
+__device__ bool table_add(uint32_t* key, uint32_t* cnt, uint32_t* distinct, uint32_t slots_log2, uint32_t w,
+                          uint32_t amount) {
+  const uint32_t slots = 1u << slots_log2;
+  const uint32_t k = w + 1;
+  uint32_t h = word_hash(w, slots_log2);
+  for (uint32_t probe = 0; probe < slots; ++probe, h = (h + 1) & (slots - 1)) {
+    uint32_t cur = key[h];
+    if (cur == 0) {
+      cur = atomicCAS(&key[h], 0u, k);
+      if (cur == 0) {
+        if (atomicAdd(distinct, 1u) >= kMaxDistinct) return false;
+        atomicAdd(&cnt[h], amount);
+        return true;
+      }
+    }
+    if (cur == k) {
+      atomicAdd(&cnt[h], amount);
+      return true;
+    }
+  }
+  return false;
+}
+
+__global__ void __launch_bounds__(kStatsThreads) stats_kernel(const BlockJob* __restrict__ jobs, PacketStats* pstats,
+                                                              BlockStats* bstats) {
+  __shared__ uint32_t hist[2][2][256];
+  __shared__ uint32_t key[2][kLocalSlots], cnt[2][kLocalSlots];
+  __shared__ uint32_t distinct[2], overflow[2];
+  __shared__ uint32_t ck[4][kStatsThreads];  // aB, bB, aA, bA per thread
+  const uint32_t t = threadIdx.x;
+  for (uint32_t i = t; i < 2 * 2 * 256; i += kStatsThreads) (&hist[0][0][0])[i] = 0;
+  for (uint32_t i = t; i < 2 * kLocalSlots; i += kStatsThreads) {
+    (&key[0][0])[i] = 0;
+    (&cnt[0][0])[i] = 0;
+  }
+  if (t < 2) {
+    distinct[t] = 0;
+    overflow[t] = 0;
+  }
+  __syncthreads();
+  const BlockJob job = jobs[blockIdx.x];
+  const uint32_t n = job.nbytes;
+  const uint32_t W = n / 2;
+  const uint32_t groups = (n + WS_GROUP_BYTES - 1) / WS_GROUP_BYTES;
+  const uint32_t chunks = (n + 15) / 16;
+  uint32_t nz = 0;
+  uint32_t aB = 0, bB = 0, aA = 0, bA = 0;
+  const bool aligned = (((uintptr_t)job.base | (uintptr_t)job.target) & 15u) == 0;
+  for (uint32_t k = t; k < chunks; k += kStatsThreads) {
+    const uint32_t g = k >> 5;  // 32 chunks of 16 bytes per 512-byte group; lane = k & 31 = t & 31
+    uint8_t ab[16], tb[16];
+    if (aligned && 16 * k + 16 <= n) {
+      *reinterpret_cast<uint4*>(ab) = *reinterpret_cast<const uint4*>(job.base + 16 * k);
+      *reinterpret_cast<uint4*>(tb) = *reinterpret_cast<const uint4*>(job.target + 16 * k);
+    } else {
+#pragma unroll
+      for (uint32_t i = 0; i < 16; ++i) {
+        ab[i] = 16 * k + i < n ? job.base[16 * k + i] : 0;
+        tb[i] = 16 * k + i < n ? job.target[16 * k + i] : 0;
+      }
+    }
+    const uint32_t* aw = reinterpret_cast<const uint32_t*>(ab);
+    const uint32_t* tw = reinterpret_cast<const uint32_t*>(tb);
+    const uint32_t sA = aw[0] + aw[1] + aw[2] + aw[3];
+    const uint32_t sB = tw[0] + tw[1] + tw[2] + tw[3];
+    aA += sA;
+    bA += (groups - g) * sA;
+    aB += sB;
+    bB += (groups - g) * sB;
+    nz |= (aw[0] ^ tw[0]) | (aw[1] ^ tw[1]) | (aw[2] ^ tw[2]) | (aw[3] ^ tw[3]);
+#pragma unroll
+    for (uint32_t j = 0; j < 8; ++j) {
+      if (8 * k + j >= W) break;
+      const uint16_t a16 = (uint16_t)(ab[2 * j] | (ab[2 * j + 1] << 8));
+      const uint16_t t16 = (uint16_t)(tb[2 * j] | (tb[2 * j + 1] << 8));
+      const uint16_t v[2] = {(uint16_t)(a16 ^ t16), u16_word(a16, t16)};
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        atomicAdd(&hist[c][0][v[c] & 0xFF], 1u);
+        atomicAdd(&hist[c][1][v[c] >> 8], 1u);
+        if (!overflow[c] && !table_add(key[c], cnt[c], &distinct[c], 9, v[c], 1)) overflow[c] = 1;
+      }
+    }
+  }
+  const bool any = __syncthreads_or(nz != 0);
+  ck[0][t] = aB;
+  ck[1][t] = bB;
+  ck[2][t] = aA;
+  ck[3][t] = bA;
+  __syncthreads();
+  BlockStats* out = bstats + blockIdx.x;
+  if (t < 32) {
+    uint32_t s[4] = {0, 0, 0, 0};
+    for (uint32_t i = t; i < kStatsThreads; i += 32)
+      for (int q = 0; q < 4; ++q) s[q] += ck[q][i];
+    unsigned long long hB = ws_lane_hash(s[0], s[1], t), hA = ws_lane_hash(s[2], s[3], t);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      hB += __shfl_xor_sync(0xFFFFFFFFu, hB, o);
+      hA += __shfl_xor_sync(0xFFFFFFFFu, hA, o);
+    }
+    if (t == 0) {
+      uint32_t tail = 0;
+      if (n & 1u) tail = (uint32_t)(job.base[n - 1] ^ job.target[n - 1]);
+      out->lane_sum[0] = hB;
+      out->lane_sum[1] = hA;
+      out->tail = tail;
+      out->nonzero = (any || tail) ? 1u : 0u;
+    }
+  }
+  // The odd tail byte alone can make a block non-zero.
+  const bool nonzero = any || ((n & 1u) && (job.base[n - 1] != job.target[n - 1]));
+  if (!nonzero) return;
+  PacketStats* ps = pstats + job.packet;
+  for (uint32_t i = t; i < 2 * 2 * 256; i += kStatsThreads) {
+    const uint32_t v = (&hist[0][0][0])[i];
+    if (v) atomicAdd(&(&ps->plane[0][0][0])[i], v);
+  }
+  for (uint32_t c = 0; c < 2; ++c) {
+    if (overflow[c]) {
+      if (t == 0) atomicExch(&ps->many[c], 1u);
+      continue;
+    }
+    for (uint32_t i = t; i < kLocalSlots; i += kStatsThreads) {
+      const uint32_t k = key[c][i];
+      if (k && !ps->many[c] && !table_add(ps->key[c], ps->cnt[c], &ps->distinct[c], 10, k - 1, cnt[c][i]))
+        atomicExch(&ps->many[c], 1u);
+    }
+  }
+}
+
+// Dictionary index table of a packet: word -> symbol.
+__global__ void dict_index_kernel(const uint16_t* __restrict__ words, uint32_t nwords, uint8_t* index) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < nwords) index[words[i]] = (uint8_t)i;
+}
+
+__device__ __forceinline__ uint32_t lanemask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+// x -> E(x, s) = (x / f) * 256 + x % f + cdf, with x / f from the reciprocal.
+__device__ __forceinline__ uint32_t rans_put(uint32_t x, uint32_t fc, uint32_t rcp) {
+  const uint32_t f = fc & 0xFFFFu, cdf = fc >> 16;
+  uint32_t q = __umulhi(x, rcp);
+  uint32_t r = x - q * f;
+  if (r >= f) {
+    ++q;
+    r -= f;
+  }
+  return (q << WS_PROB_BITS) + r + cdf;
+}
+
+__global__ void __launch_bounds__(kEncWarps * 32) encode_kernel(const BlockJob* __restrict__ blocks,
+                                                                const EncodeJob* __restrict__ jobs, uint32_t njobs,
+                                                                const EncTable* __restrict__ tables,
+                                                                const uint8_t* const* __restrict__ dict_index,
+                                                                uint16_t* out, uint32_t* nwords_out) {
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  const uint32_t j = blockIdx.x * kEncWarps + warp;
+  if (j >= njobs) return;
+  const EncodeJob job = jobs[j];
+  const BlockJob blk = blocks[job.block];
+  const EncTable& tab = tables[job.table];
+  const uint8_t* idx = job.dict ? dict_index[job.table] : nullptr;
+  uint16_t* o = out + (uint64_t)j * kOutHalfwords;
+  const uint32_t W = blk.nbytes / 2;
+  const uint32_t groups = (W + WS_GROUP_WORDS - 1) / WS_GROUP_WORDS;
+  const uint32_t cpg = job.dict ? 2u : 4u;
+  const uint32_t ltm = lanemask_lt();
+  const bool aligned = (((uintptr_t)blk.base | (uintptr_t)blk.target) & 15u) == 0;
+  uint32_t x[2] = {WS_RANS_L, WS_RANS_L};
+  uint32_t cursor = kOutHalfwords;
+  for (uint32_t g = groups; g-- > 0;) {
+    // The lane's 8 residual words of this group and their symbols per state.
+    const uint32_t w0 = g * WS_GROUP_WORDS + lane * WS_WORDS_PER_LANE;
+    uint16_t v[8];
+    if (w0 + 8 <= W && aligned) {
+      uint4 av = *reinterpret_cast<const uint4*>(blk.base + 2 * w0);
+      uint4 tv = *reinterpret_cast<const uint4*>(blk.target + 2 * w0);
+      const uint16_t* a16 = reinterpret_cast<const uint16_t*>(&av);
+      const uint16_t* t16 = reinterpret_cast<const uint16_t*>(&tv);
+#pragma unroll
+      for (uint32_t q = 0; q < 8; ++q) v[q] = job.u16 ? u16_word(a16[q], t16[q]) : (uint16_t)(a16[q] ^ t16[q]);
+    } else {
+#pragma unroll
+      for (uint32_t q = 0; q < 8; ++q) {
+        v[q] = 0;
+        if (w0 + q < W) {
+          const uint16_t a16 = (uint16_t)(blk.base[2 * (w0 + q)] | (blk.base[2 * (w0 + q) + 1] << 8));
+          const uint16_t t16 = (uint16_t)(blk.target[2 * (w0 + q)] | (blk.target[2 * (w0 + q) + 1] << 8));
+          v[q] = job.u16 ? u16_word(a16, t16) : (uint16_t)(a16 ^ t16);
+        }
+      }
+    }
+    for (uint32_t c = cpg; c-- > 0;) {
+      uint32_t sa[2], sb[2];
+      bool pa[2], pb[2];
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        uint32_t ja, jb;
+        if (job.dict) {
+          ja = 4 * c + p;
+          jb = 4 * c + 2 + p;
+        } else {
+          ja = 2 * c;
+          jb = 2 * c + 1;
+        }
+        pa[p] = w0 + ja < W;
+        pb[p] = w0 + jb < W;
+        if (job.dict) {
+          sa[p] = pa[p] ? idx[v[ja]] : 0;
+          sb[p] = pb[p] ? idx[v[jb]] : 0;
+        } else {
+          sa[p] = p ? (v[ja] >> 8) : (v[ja] & 0xFFu);
+          sb[p] = p ? (v[jb] >> 8) : (v[jb] & 0xFFu);
+        }
+      }
+      // Emission (decoder reads after decoding a then b): valid pre-images of
+      // the pair are [fa*fb, 2^16*fa*fb), of a single symbol [2^8 f, 2^24 f).
+      bool emit[2];
+      uint32_t word[2];
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        emit[p] = false;
+        word[p] = 0;
+        if (pa[p]) {
+          const uint32_t fa = tab.fc[p][sa[p]] & 0xFFFFu;
+          uint64_t xmax;
+          if (pb[p])
+            xmax = ((uint64_t)fa * (tab.fc[p][sb[p]] & 0xFFFFu)) << 16;
+          else
+            xmax = (uint64_t)fa << 24;
+          if ((uint64_t)x[p] >= xmax) {
+            emit[p] = true;
+            word[p] = x[p] & 0xFFFFu;
+            x[p] >>= 16;
+          }
+        }
+      }
+      const uint32_t e0 = __ballot_sync(0xFFFFFFFFu, emit[0]);
+      const uint32_t e1 = __ballot_sync(0xFFFFFFFFu, emit[1]);
+      const uint32_t n0 = __popc(e0);
+      const uint32_t start = cursor - n0 - __popc(e1);
+      if (emit[0]) o[start + __popc(e0 & ltm)] = (uint16_t)word[0];
+      if (emit[1]) o[start + n0 + __popc(e1 & ltm)] = (uint16_t)word[1];
+      cursor = start;
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        if (pb[p]) x[p] = rans_put(x[p], tab.fc[p][sb[p]], tab.rcp[p][sb[p]]);
+        if (pa[p]) x[p] = rans_put(x[p], tab.fc[p][sa[p]], tab.rcp[p][sa[p]]);
+      }
+    }
+  }
+  uint32_t* hdr = reinterpret_cast<uint32_t*>(o);
+  hdr[lane] = x[0];
+  hdr[32 + lane] = x[1];
+  if (lane == 0) nwords_out[j] = WS_HEADER_HALFWORDS + (kOutHalfwords - cursor);
+}
+
+// Packs one block's payload (ANS header + stream, or raw XOR bytes) at dst,
+// zero-padded to 16 bytes.
+__global__ void compact_kernel(const CompactJob* __restrict__ jobs, const BlockJob* __restrict__ blocks,
+                               const uint16_t* __restrict__ enc_out, uint8_t* out) {
+  const CompactJob job = jobs[blockIdx.x];
+  const BlockJob blk = blocks[job.block];
+  uint8_t* d = out + job.dst;
+  if (job.encode == ~0u) {
+    const uint32_t n = blk.nbytes, padded = (n + 15) & ~15u;
+    for (uint32_t i = threadIdx.x; i < padded; i += blockDim.x) d[i] = i < n ? (uint8_t)(blk.base[i] ^ blk.target[i]) : 0;
+    return;
+  }
+  const uint16_t* src = enc_out + (uint64_t)job.encode * kOutHalfwords;
+  const uint32_t stream = job.nwords - WS_HEADER_HALFWORDS;
+  const uint32_t first = kOutHalfwords - stream;
+  uint16_t* d16 = reinterpret_cast<uint16_t*>(d);
+  const uint32_t padded_hw = ((2 * job.nwords + 15) & ~15u) / 2;
+  for (uint32_t i = threadIdx.x; i < padded_hw; i += blockDim.x) {
+    uint16_t v = 0;
+    if (i < WS_HEADER_HALFWORDS)
+      v = src[i];
+    else if (i < job.nwords)
+      v = src[first + (i - WS_HEADER_HALFWORDS)];
+    d16[i] = v;
+  }
+}
+
+template <class T>
+struct DeviceBuffer {
+  T* ptr = nullptr;
+  size_t count = 0;
+  cudaError_t ensure(size_t n) {
+    if (n <= count) return cudaSuccess;
+    if (ptr) cudaFree(ptr);
+    ptr = nullptr;
+    count = 0;
+    cudaError_t e = cudaMalloc((void**)&ptr, std::max<size_t>(n, 1) * sizeof(T));
+    if (e == cudaSuccess) count = n;
+    return e;
+  }
+  ~DeviceBuffer() {
+    if (ptr) cudaFree(ptr);
+  }
+};
+
+uint32_t reciprocal(uint32_t f) { return f <= 1 ? 0xFFFFFFFFu : (uint32_t)((1ull << 32) / f); }
+
+void fill_enc_table(const CodingTables& ct, EncTable* t) {
+  for (int p = 0; p < 2; ++p)
+    for (int s = 0; s < 256; ++s) {
+      t->fc[p][s] = ct.freq[p][s] | (ct.cdf[p][s] << 16);
+      t->rcp[p][s] = reciprocal(ct.freq[p][s]);
+    }
+}
+
+}  // namespace
+
+#define WS_GPU_TRY(expr)                                                             \
+  do {                                                                               \
+    cudaError_t e_ = (expr);                                                         \
+    if (e_ != cudaSuccess) {                                                         \
+      *err = std::string("GPU encoder: ") + #expr + ": " + cudaGetErrorString(e_);   \
+      return false;                                                                  \
+    }                                                                                \
+  } while (0)
+
+bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, int dict_slack_pct,
+                        uint64_t batch_bytes, cudaStream_t stream, std::vector<EncodedPacket>* out, std::string* err) {
+  out->resize(packets.size());
+  DeviceBuffer<uint8_t> d_base, d_payload, d_index;
+  DeviceBuffer<BlockJob> d_blocks;
+  DeviceBuffer<PacketStats> d_pstats;
+  DeviceBuffer<BlockStats> d_bstats;
+  DeviceBuffer<EncodeJob> d_jobs;
+  DeviceBuffer<EncTable> d_tables;
+  DeviceBuffer<const uint8_t*> d_index_ptrs;
+  DeviceBuffer<uint16_t> d_enc;
+  DeviceBuffer<uint32_t> d_nwords;
+  DeviceBuffer<CompactJob> d_compact;
+  DeviceBuffer<uint16_t> d_words;
+  size_t first = 0;
+  while (first < packets.size()) {
+    // One batch: consecutive packets up to batch_bytes of weights.
+    size_t last = first;
+    uint64_t bytes = 0;
+    while (last < packets.size() && (last == first || bytes + packets[last].nbytes <= batch_bytes))
+      bytes += (packets[last++].nbytes + 255) & ~255ull;  // packets start 256-byte aligned in the device copy
+    const size_t np = last - first;
+    WS_GPU_TRY(d_base.ensure(bytes));
+    std::vector<BlockJob> blocks;
+    std::vector<uint32_t> packet_first_block(np + 1);
+    uint64_t off = 0;
+    for (size_t i = 0; i < np; ++i) {
+      const GpuPacketInput& p = packets[first + i];
+      WS_GPU_TRY(cudaMemcpyAsync(d_base.ptr + off, p.base, p.nbytes, cudaMemcpyHostToDevice, stream));
+      packet_first_block[i] = (uint32_t)blocks.size();
+      for (uint64_t b = 0; b < p.nbytes; b += WS_BLOCK_BYTES)
+        blocks.push_back(BlockJob{d_base.ptr + off + b, p.target + b,
+                                  (uint32_t)std::min<uint64_t>(WS_BLOCK_BYTES, p.nbytes - b), (uint32_t)i});
+      off += (p.nbytes + 255) & ~255ull;
+    }
+    packet_first_block[np] = (uint32_t)blocks.size();
+    const size_t nb = blocks.size();
+    WS_GPU_TRY(d_blocks.ensure(nb));
+    WS_GPU_TRY(d_pstats.ensure(np));
+    WS_GPU_TRY(d_bstats.ensure(nb));
+    WS_GPU_TRY(cudaMemcpyAsync(d_blocks.ptr, blocks.data(), nb * sizeof(BlockJob), cudaMemcpyHostToDevice, stream));
+    WS_GPU_TRY(cudaMemsetAsync(d_pstats.ptr, 0, np * sizeof(PacketStats), stream));
+    if (nb) {
+      stats_kernel<<<(unsigned)nb, kStatsThreads, 0, stream>>>(d_blocks.ptr, d_pstats.ptr, d_bstats.ptr);
+      WS_GPU_TRY(cudaGetLastError());
+    }
+    std::vector<PacketStats> pstats(np);
+    std::vector<BlockStats> bstats(nb);
+    WS_GPU_TRY(cudaMemcpyAsync(pstats.data(), d_pstats.ptr, np * sizeof(PacketStats), cudaMemcpyDeviceToHost, stream));
+    WS_GPU_TRY(cudaMemcpyAsync(bstats.data(), d_bstats.ptr, nb * sizeof(BlockStats), cudaMemcpyDeviceToHost, stream));
+    WS_GPU_TRY(cudaStreamSynchronize(stream));
+
+    // Tables per packet and candidate (host, shared code with the host encoder).
+    struct Cand {
+      int table = -1;
+      bool dict = false;
+    };
+    std::vector<Cand> cand(np * 2);
+    std::vector<EncTable> tables;
+    std::vector<std::vector<uint16_t>> dict_words;
+    std::vector<int> dict_of_table;
+    std::vector<EncodeJob> jobs;
+    std::vector<std::vector<uint32_t>> job_of(np * 2);
+    std::vector<CodingTables> coding(np * 2);
+    std::vector<char> skip(np, 0);
+    for (size_t i = 0; i < np; ++i) {
+      const GpuPacketInput& p = packets[first + i];
+      EncodedPacket& e = (*out)[first + i];
+      e.nbytes = p.nbytes;
+      e.blocks.clear();
+      e.zero_block_bytes = 0;
+      e.payload_bytes = 0;
+      bool any = false;
+      uint32_t coded = 0;
+      for (uint32_t b = packet_first_block[i]; b < packet_first_block[i + 1]; ++b) {
+        if (bstats[b].nonzero) {
+          any = true;
+          ++coded;
+        } else {
+          e.zero_block_bytes += blocks[b].nbytes;
+        }
+      }
+      if (p.nbytes == 0 || !any) {  // delta.py:181-182: unchanged chunk
+        e.mode = WS_MODE_SKIP;
+        e.zero_block_bytes = 0;
+        skip[i] = 1;
+        continue;
+      }
+      const bool big = p.nbytes >= WS_COMPRESS_MIN;
+      const bool try_c[2] = {big && !(policy == 2 && p.is_bf16), big && p.is_bf16 && (p.nbytes % 2 == 0) && policy != 1};
+      for (int c = 0; c < 2; ++c) {
+        if (!try_c[c]) continue;
+        const PacketStats& ps = pstats[i];
+        uint64_t counts[2][256];
+        for (int q = 0; q < 2; ++q)
+          for (int s = 0; s < 256; ++s) counts[q][s] = ps.plane[c][q][s];
+        std::vector<std::pair<uint16_t, uint64_t>> wl;
+        const bool many = ps.many[c] != 0;
+        if (!many)
+          for (uint32_t k = 0; k < kPacketSlots; ++k)
+            if (ps.key[c][k]) wl.emplace_back((uint16_t)(ps.key[c][k] - 1), ps.cnt[c][k]);
+        std::sort(wl.begin(), wl.end());
+        std::vector<uint16_t> words;
+        std::vector<uint64_t> wcounts;
+        for (auto& pr : wl) {
+          words.push_back(pr.first);
+          wcounts.push_back(pr.second);
+        }
+        CodingTables& ct = coding[2 * i + c];
+        choose_coding(counts, words, wcounts, many || words.size() > 255, coded, dict_slack_pct, &ct);
+        Cand& cd = cand[2 * i + c];
+        cd.table = (int)tables.size();
+        cd.dict = ct.dict;
+        EncTable et;
+        fill_enc_table(ct, &et);
+        tables.push_back(et);
+        dict_of_table.push_back(ct.dict ? (int)dict_words.size() : -1);
+        if (ct.dict) dict_words.push_back(ct.words);
+        for (uint32_t b = packet_first_block[i]; b < packet_first_block[i + 1]; ++b) {
+          if (!bstats[b].nonzero) continue;
+          job_of[2 * i + c].push_back((uint32_t)jobs.size());
+          jobs.push_back(EncodeJob{b, (uint32_t)cd.table, ct.dict ? 1u : 0u, (uint32_t)c});
+        }
+      }
+    }
+    // Encode every candidate block.
+    std::vector<uint32_t> nwords(jobs.size());
+    if (!jobs.empty()) {
+      WS_GPU_TRY(d_tables.ensure(tables.size()));
+      WS_GPU_TRY(cudaMemcpyAsync(d_tables.ptr, tables.data(), tables.size() * sizeof(EncTable), cudaMemcpyHostToDevice, stream));
+      WS_GPU_TRY(d_index.ensure(std::max<size_t>(1, dict_words.size()) * 65536));
+      WS_GPU_TRY(d_words.ensure(std::max<size_t>(1, dict_words.size()) * 256));
+      std::vector<const uint8_t*> index_ptrs(tables.size(), nullptr);
+      for (size_t t = 0; t < tables.size(); ++t) {
+        const int d = dict_of_table[t];
+        if (d < 0) continue;
+        index_ptrs[t] = d_index.ptr + (size_t)d * 65536;
+        uint16_t* dw = d_words.ptr + (size_t)d * 256;
+        WS_GPU_TRY(cudaMemcpyAsync(dw, dict_words[d].data(), dict_words[d].size() * 2, cudaMemcpyHostToDevice, stream));
+        dict_index_kernel<<<1, 256, 0, stream>>>(dw, (uint32_t)dict_words[d].size(), d_index.ptr + (size_t)d * 65536);
+        WS_GPU_TRY(cudaGetLastError());
+      }
+      WS_GPU_TRY(d_index_ptrs.ensure(tables.size()));
+      WS_GPU_TRY(cudaMemcpyAsync(d_index_ptrs.ptr, index_ptrs.data(), tables.size() * sizeof(void*), cudaMemcpyHostToDevice, stream));
+      WS_GPU_TRY(d_jobs.ensure(jobs.size()));
+      WS_GPU_TRY(cudaMemcpyAsync(d_jobs.ptr, jobs.data(), jobs.size() * sizeof(EncodeJob), cudaMemcpyHostToDevice, stream));
+      WS_GPU_TRY(d_enc.ensure(jobs.size() * (size_t)kOutHalfwords));
+      WS_GPU_TRY(d_nwords.ensure(jobs.size()));
+      const unsigned grid = (unsigned)((jobs.size() + kEncWarps - 1) / kEncWarps);
+      encode_kernel<<<grid, kEncWarps * 32, 0, stream>>>(d_blocks.ptr, d_jobs.ptr, (uint32_t)jobs.size(), d_tables.ptr,
+                                                         d_index_ptrs.ptr, d_enc.ptr, d_nwords.ptr);
+      WS_GPU_TRY(cudaGetLastError());
+      WS_GPU_TRY(cudaMemcpyAsync(nwords.data(), d_nwords.ptr, jobs.size() * 4, cudaMemcpyDeviceToHost, stream));
+      WS_GPU_TRY(cudaStreamSynchronize(stream));
+    }
+    // Mode rule (delta.py:184-193) and raw fallback, then pack the chosen payloads.
+    std::vector<CompactJob> compact;
+    struct Pending {
+      size_t packet, block_index;
+    };
+    std::vector<Pending> pending;
+    uint64_t out_bytes = 0;
+    for (size_t i = 0; i < np; ++i) {
+      EncodedPacket& e = (*out)[first + i];
+      if (skip[i]) continue;
+      const uint64_t n = packets[first + i].nbytes;
+      int mode = WS_MODE_XOR_RAW, best_c = -1;
+      uint64_t best = n;
+      for (int c = 0; c < 2; ++c) {
+        if (cand[2 * i + c].table < 0) continue;
+        uint64_t size = 1024;
+        for (uint32_t jj : job_of[2 * i + c]) {
+          const uint32_t ans = (2 * nwords[jj] + 15) & ~15u;
+          const uint32_t raw = (blocks[jobs[jj].block].nbytes + 15) & ~15u;
+          size += ans < raw ? ans : raw;
+        }
+        if (size < best) {
+          best = size;
+          best_c = c;
+          mode = c == 1 ? WS_MODE_U16_ANS : ((n % 2 == 0) ? WS_MODE_XOR_GROUP2_ANS : WS_MODE_XOR_ANS);
+        }
+      }
+      e.mode = mode;
+      e.payload_bytes = best;
+      if (best_c >= 0)
+        memcpy(e.table, coding[2 * i + best_c].entries, sizeof(e.table));
+      else
+        memset(e.table, 0, sizeof(e.table));
+      size_t jpos = 0;
+      for (uint32_t b = packet_first_block[i]; b < packet_first_block[i + 1]; ++b) {
+        if (!bstats[b].nonzero) continue;
+        EncodedBlock blk;
+        blk.offset = (b - packet_first_block[i]) * WS_BLOCK_BYTES;
+        blk.nbytes = blocks[b].nbytes;
+        blk.tail = 0;
+        blk.flags = 0;
+        blk.nwords = 0;
+        blk.kind = WS_KIND_RAW;
+        blk.lane_sum[0] = bstats[b].lane_sum[0];
+        blk.lane_sum[1] = bstats[b].lane_sum[1];
+        const uint32_t raw = (blk.nbytes + 15) & ~15u;
+        CompactJob cj{b, ~0u, 0, 0, out_bytes};
+        uint32_t size = raw;
+        if (best_c >= 0) {
+          const uint32_t jj = job_of[2 * i + best_c][jpos];
+          const uint32_t ans = (2 * nwords[jj] + 15) & ~15u;
+          if (ans < raw) {
+            const bool dict = cand[2 * i + best_c].dict;
+            blk.kind = best_c == 1 ? (dict ? WS_KIND_DICT_U16 : WS_KIND_ANS_U16)
+                                   : (dict ? WS_KIND_DICT_XOR : WS_KIND_ANS_XOR);
+            blk.nwords = nwords[jj];
+            if (blk.nbytes & 1u) {
+              blk.flags = WS_FLAG_ODD_TAIL;
+              blk.tail = (uint8_t)bstats[b].tail;
+            }
+            cj.encode = jj;
+            cj.nwords = nwords[jj];
+            size = ans;
+          }
+        }
+        ++jpos;
+        blk.payload.assign(size, 0);
+        compact.push_back(cj);
+        pending.push_back(Pending{first + i, e.blocks.size()});
+        out_bytes += size;
+        e.blocks.push_back(std::move(blk));
+      }
+    }
+    if (!compact.empty()) {
+      WS_GPU_TRY(d_compact.ensure(compact.size()));
+      WS_GPU_TRY(d_payload.ensure(out_bytes));
+      WS_GPU_TRY(cudaMemcpyAsync(d_compact.ptr, compact.data(), compact.size() * sizeof(CompactJob), cudaMemcpyHostToDevice, stream));
+      compact_kernel<<<(unsigned)compact.size(), 256, 0, stream>>>(d_compact.ptr, d_blocks.ptr, d_enc.ptr, d_payload.ptr);
+      WS_GPU_TRY(cudaGetLastError());
+      std::vector<uint8_t> host(out_bytes);
+      WS_GPU_TRY(cudaMemcpyAsync(host.data(), d_payload.ptr, out_bytes, cudaMemcpyDeviceToHost, stream));
+      WS_GPU_TRY(cudaStreamSynchronize(stream));
+      for (size_t k = 0; k < compact.size(); ++k) {
+        EncodedBlock& blk = (*out)[pending[k].packet].blocks[pending[k].block_index];
+        memcpy(blk.payload.data(), host.data() + compact[k].dst, blk.payload.size());
+      }
+    }
+    first = last;
+  }
+  return true;
+}
+
+}  // namespace ws

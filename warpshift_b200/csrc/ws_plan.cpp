@@ -25,6 +25,7 @@
 #include "../../include/warpshift_b200.h"
 #include "ws_encoder.h"
 #include "ws_format.h"
+#include "ws_gpu_encoder.h"
 #include "ws_kernels.h"
 
 namespace {
@@ -159,6 +160,19 @@ int encode_all(const ws_tensor_desc* tensors, const std::vector<PacketRef>& pack
                cudaStream_t stream, std::vector<ws::EncodedPacket>* out) {
   const int threads = o.threads > 0 ? o.threads : default_threads();
   out->resize(packets.size());
+  if (o.target_on_device && o.encode_on_device) {
+    std::vector<ws::GpuPacketInput> in;
+    in.reserve(packets.size());
+    for (const PacketRef& pr : packets) {
+      const ws_tensor_desc& t = tensors[pr.tensor];
+      in.push_back(ws::GpuPacketInput{(const uint8_t*)t.base + pr.offset, (const uint8_t*)t.target + pr.offset,
+                                      pr.nbytes, t.is_bf16 != 0});
+    }
+    std::string err;
+    if (!ws::gpu_encode_packets(in, o.policy, o.dict_slack_pct, 512ull << 20, stream, out, &err))
+      return fail(WS_ERR_CUDA, err);
+    return WS_OK;
+  }
   if (!o.target_on_device) {
     parallel_for(packets.size(), threads, [&](uint64_t i) {
       const PacketRef& pr = packets[i];

@@ -90,6 +90,7 @@ class DeltaWeights:
         batch_bytes: int = _STAGING_BATCH_BYTES,
         staging_slots: int = 3,
         dict_slack_pct: int = _DICT_SLACK_PCT,
+        encode_on_device: bool = True,
     ) -> None:
         started = time.perf_counter()
         if policy not in _lib.POLICIES:
@@ -119,6 +120,7 @@ class DeltaWeights:
             staging_slots=staging_slots,
             pin_arena=1,
             dict_slack_pct=dict_slack_pct,
+            encode_on_device=int(bool(encode_on_device)),
         )
         plan = ctypes.c_void_p()
         with torch.cuda.device(self.device):
@@ -148,6 +150,7 @@ class DeltaWeights:
             # Additions of this implementation.
             "policy": policy,
             "dict_slack_pct": dict_slack_pct,
+            "encoder": "gpu" if encode_on_device else "host",
             "block_bytes": _BLOCK_BYTES,
             "touched_bytes": int(native.touched_bytes),
             "zero_block_bytes": int(native.zero_block_bytes),
