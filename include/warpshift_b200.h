@@ -65,6 +65,8 @@ typedef struct ws_build_options {
                                above the byte-plane coding; negative: byte planes only */
   int32_t encode_on_device; /* 1 (with target_on_device): compute statistics and encode on the GPU,
                                copying only A host->device; 0: copy B device->host, encode on host threads */
+  uint64_t encode_batch_bytes; /* GPU encoder: weight bytes encoded per device batch (0 = 512 MiB); the
+                                  device holds up to about 4x this in temporary buffers during prepare */
 } ws_build_options;
 
 typedef struct ws_plan_stats {
@@ -101,7 +103,10 @@ typedef struct ws_plan_view {
   uint64_t ntiles;
   const uint32_t* tables; /* 512 slot entries per packet table */
   uint64_t ntables;
-  const uint8_t* arena;   /* host arena holding every block payload */
+  const uint8_t* arena;   /* host arena holding every block payload; when the plan keeps
+                             its arena in several host chunks (GPU encoder: one per
+                             encode_batch_bytes of weights), the first call makes one contiguous
+                             copy that lives as long as the plan */
   uint64_t arena_bytes;
 } ws_plan_view;
 
@@ -117,9 +122,13 @@ WS_API int ws_u16_residual(const uint8_t* base, const uint8_t* target, uint64_t 
 
 /* Replaces the prepare half of DeltaWeights.__init__ (delta.py:102-135: _bind_tensors'
  * overlap check 137-162, _encode_packets 196-216, _encode_chunk 176-194, _compress
- * 164-174, _prepare_batches/_pack_batch 218-280). Copies B device->host in 16 MiB
- * packets on `stream`, encodes every packet on `threads` host threads, lays out the
- * arena and descriptors. Allocates no device memory. */
+ * 164-174, _prepare_batches/_pack_batch 218-280). With target_on_device and
+ * encode_on_device, A is copied host->device in encode_batch_bytes batches (pageable A staged
+ * through pinned buffers by up to `threads` host threads) and every packet is
+ * encoded on the device on `stream`; the payloads come back into the host arena and
+ * the temporary device buffers are freed before returning. Otherwise B is copied
+ * device->host in 16 MiB packets and encoded on `threads` host threads. Both
+ * encoders produce byte-identical plans. */
 WS_API int ws_plan_build(const ws_tensor_desc* tensors, uint64_t ntensors, const ws_build_options* opts,
                   void* stream, ws_plan** out);
 

@@ -20,15 +20,16 @@ from warpshift_b200 import _lib
 pytestmark = pytest.mark.gpu
 
 
-def build(a, b_dev, policy, slack, on_device):
+def build(a, b_dev, policy, slack, on_device, encode_batch_bytes=0, pin_arena=0, batch_bytes=0):
     lib = _lib.load()
     descs = (_lib.TensorDesc * len(a))()
     for i, name in enumerate(b_dev):
         t = b_dev[name]
         descs[i] = _lib.TensorDesc(a[name].data_ptr(), t.data_ptr(), t.numel() * t.element_size(),
                                    int(t.dtype == torch.bfloat16), 0)
-    opts = _lib.BuildOptions(policy=_lib.POLICIES[policy], threads=4, target_on_device=1, device=0, batch_bytes=0,
-                             staging_slots=0, pin_arena=0, dict_slack_pct=slack, encode_on_device=int(on_device))
+    opts = _lib.BuildOptions(policy=_lib.POLICIES[policy], threads=4, target_on_device=1, device=0,
+                             batch_bytes=batch_bytes, staging_slots=0, pin_arena=pin_arena, dict_slack_pct=slack,
+                             encode_on_device=int(on_device), encode_batch_bytes=encode_batch_bytes)
     plan = ctypes.c_void_p()
     stream = torch.cuda.current_stream().cuda_stream
     _lib.check(lib.ws_plan_build(descs, len(a), ctypes.byref(opts), stream, ctypes.byref(plan)))
@@ -77,3 +78,47 @@ def test_gpu_encoder_matches_on_unaligned_views_and_many_packets(cuda_device) ->
         finally:
             lib.ws_plan_destroy(p_gpu)
             lib.ws_plan_destroy(p_host)
+
+
+def test_gpu_encoder_matches_with_pinned_base(cuda_device) -> None:
+    """Page-locked A goes to the device by DMA alone, without the staging threads."""
+    a, b = edge_pair(seed=17)
+    a_pinned = {k: v.pin_memory() for k, v in a.items()}
+    b_dev = {k: v.to(cuda_device) for k, v in b.items()}
+    lib = _lib.load()
+    p_gpu = build(a_pinned, b_dev, "auto", 6, True)
+    p_host = build(a, b_dev, "auto", 6, False)
+    try:
+        assert_same_plan(p_gpu, p_host)
+    finally:
+        lib.ws_plan_destroy(p_gpu)
+        lib.ws_plan_destroy(p_host)
+
+
+def test_gpu_encoder_arena_in_several_chunks(cuda_device) -> None:
+    """16 MiB encoder batches over ~72 MiB of weights: five arena chunks. The plan,
+    its contiguous view and a staged forward/reverse apply over the chunks match."""
+    x, y = bf16_pair((72 << 20) // 2 + 77, 0.01, 5)
+    x2, y2 = bf16_pair((3 << 20) // 2, 0.01, 6)
+    a = {"w": x, "v": x2}
+    b_dev = {"w": y.to(cuda_device), "v": y2.to(cuda_device)}
+    lib = _lib.load()
+    p_gpu = build(a, b_dev, "auto", 6, True, encode_batch_bytes=16 << 20, pin_arena=1, batch_bytes=3 << 20)
+    p_host = build(a, b_dev, "auto", 6, False, pin_arena=1, batch_bytes=3 << 20)
+    try:
+        assert_same_plan(p_gpu, p_host)
+        stats = _lib.PlanStats()
+        _lib.check(lib.ws_plan_get_stats(p_gpu, ctypes.byref(stats)))
+        stream = torch.cuda.current_stream().cuda_stream
+        _lib.check(lib.ws_plan_upload(p_gpu, stream))
+        res = _lib.ApplyResult()
+        _lib.check(lib.ws_apply(p_gpu, 1, stream, None, ctypes.byref(res)))  # B -> A
+        assert res.launches == stats.batches > 1
+        for k in a:
+            assert torch.equal(b_dev[k].cpu().view(torch.int16), a[k].view(torch.int16)), k
+        _lib.check(lib.ws_apply(p_gpu, 0, stream, None, ctypes.byref(res)))  # A -> B
+        assert torch.equal(b_dev["w"].cpu().view(torch.int16), y.view(torch.int16))
+        assert torch.equal(b_dev["v"].cpu().view(torch.int16), y2.view(torch.int16))
+    finally:
+        lib.ws_plan_destroy(p_gpu)
+        lib.ws_plan_destroy(p_host)

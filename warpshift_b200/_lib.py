@@ -35,6 +35,7 @@ class BuildOptions(ctypes.Structure):
         ("pin_arena", i32),
         ("dict_slack_pct", i32),
         ("encode_on_device", i32),
+        ("encode_batch_bytes", u64),
     ]
 
 

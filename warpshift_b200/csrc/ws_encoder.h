@@ -17,6 +17,7 @@ struct EncodedBlock {
   uint8_t flags;
   uint32_t nwords;  // ANS stream halfwords incl. header (0 for RAW)
   std::vector<uint8_t> payload;  // padded to WS_PAYLOAD_ALIGN
+  uint32_t clen = 0;             // payload bytes when the payload is held in an arena chunk instead
   uint64_t lane_sum[2];          // checksum lane sums of the bytes written: [0] forward (B), [1] reverse (A)
 };
 

@@ -16,9 +16,17 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <string.h>
+#include <sys/mman.h>
+
+#include <stdio.h>
+#include <stdlib.h>
 
 #include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "ws_encoder.h"
@@ -404,7 +412,197 @@ void fill_enc_table(const CodingTables& ct, EncTable* t) {
     }
 }
 
+double seconds_since(std::chrono::steady_clock::time_point t) {
+  return std::chrono::duration<double>(std::chrono::steady_clock::now() - t).count();
+}
+
+// Host -> device copies of A for one batch, issued on the uploader's own
+// streams. Pinned (page-locked or registered) sources are copied by the DMA
+// engine directly; pageable ones are staged by host threads, each copying into
+// one of its two pinned slots while the DMA of the other slot runs. copy()
+// starts after `after` (the event that releases the destination buffer);
+// order_before() makes `stream` wait for the copies.
+class Uploader {
+ public:
+  struct Piece {
+    uint8_t* dst;
+    const uint8_t* src;
+    uint64_t bytes;
+  };
+  static constexpr uint64_t kSlotBytes = 16ull << 20;
+
+  Uploader(int device, int threads) : device_(device), nworkers_(std::max(1, std::min(threads, 8))) {}
+  ~Uploader() {
+    cudaSetDevice(device_);
+    for (Worker& w : workers_) {
+      if (w.stream) cudaStreamSynchronize(w.stream);
+      for (int k = 0; k < 2; ++k) {
+        if (w.slot[k]) cudaFreeHost(w.slot[k]);
+        if (w.ev[k]) cudaEventDestroy(w.ev[k]);
+      }
+      if (w.done) cudaEventDestroy(w.done);
+      if (w.stream) cudaStreamDestroy(w.stream);
+    }
+  }
+
+  cudaError_t copy(const std::vector<Piece>& pieces, cudaEvent_t after) {
+    used_ = 0;
+    cudaError_t e = cudaSetDevice(device_);
+    if (e == cudaSuccess) e = ensure_workers(1);
+    if (e != cudaSuccess) return e;
+    std::vector<Piece> staged;
+    std::vector<Piece> direct;
+    for (const Piece& pc : pieces) {
+      cudaPointerAttributes attr;
+      e = cudaPointerGetAttributes(&attr, pc.src);
+      if (e != cudaSuccess) cudaGetLastError();  // unknown host memory: treat as pageable
+      if (e == cudaSuccess && attr.type == cudaMemoryTypeHost) {
+        direct.push_back(pc);
+      } else {
+        for (uint64_t o = 0; o < pc.bytes; o += kSlotBytes)
+          staged.push_back(Piece{pc.dst + o, pc.src + o, std::min(kSlotBytes, pc.bytes - o)});
+      }
+    }
+    const size_t nw = std::max<size_t>(1, std::min<size_t>((size_t)nworkers_, staged.size()));
+    e = ensure_workers(nw);
+    for (size_t w = 0; w < nw && e == cudaSuccess; ++w) e = cudaStreamWaitEvent(workers_[w].stream, after, 0);
+    for (const Piece& pc : direct) {
+      if (e != cudaSuccess) break;
+      e = cudaMemcpyAsync(pc.dst, pc.src, pc.bytes, cudaMemcpyHostToDevice, workers_[0].stream);
+    }
+    if (e != cudaSuccess) return e;
+    std::atomic<size_t> next{0};
+    std::mutex mu;
+    cudaError_t first_error = cudaSuccess;
+    auto body = [&](size_t w) {
+      Worker& wk = workers_[w];
+      cudaError_t err = cudaSetDevice(device_);
+      for (size_t i = next++; i < staged.size() && err == cudaSuccess; i = next++) {
+        const int k = wk.turn;
+        wk.turn ^= 1;
+        const auto tw = std::chrono::steady_clock::now();
+        err = cudaEventSynchronize(wk.ev[k]);  // the slot's previous DMA is done
+        wk.wait_seconds += seconds_since(tw);
+        if (err != cudaSuccess) break;
+        const auto t0 = std::chrono::steady_clock::now();
+        memcpy(wk.slot[k], staged[i].src, staged[i].bytes);
+        wk.memcpy_seconds += seconds_since(t0);
+        err = cudaMemcpyAsync(staged[i].dst, wk.slot[k], staged[i].bytes, cudaMemcpyHostToDevice, wk.stream);
+        if (err == cudaSuccess) err = cudaEventRecord(wk.ev[k], wk.stream);
+      }
+      if (err != cudaSuccess) {
+        std::lock_guard<std::mutex> lk(mu);
+        if (first_error == cudaSuccess) first_error = err;
+      }
+    };
+    std::vector<std::thread> pool;
+    for (size_t w = 1; w < nw; ++w) pool.emplace_back(body, w);
+    body(0);
+    for (auto& t : pool) t.join();
+    if (first_error != cudaSuccess) return first_error;
+    for (size_t w = 0; w < nw; ++w) {
+      e = cudaEventRecord(workers_[w].done, workers_[w].stream);
+      if (e != cudaSuccess) return e;
+    }
+    used_ = nw;
+    return cudaSuccess;
+  }
+
+  // Work queued on `stream` after this call starts once the last copy() is done.
+  cudaError_t order_before(cudaStream_t stream) {
+    for (size_t w = 0; w < used_; ++w) {
+      cudaError_t e = cudaStreamWaitEvent(stream, workers_[w].done, 0);
+      if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+  }
+
+  // Thread-seconds spent copying into slots and waiting for slots, summed over workers.
+  void busy(double* memcpy_s, double* wait_s) const {
+    *memcpy_s = *wait_s = 0;
+    for (const Worker& w : workers_) {
+      *memcpy_s += w.memcpy_seconds;
+      *wait_s += w.wait_seconds;
+    }
+  }
+
+ private:
+  struct Worker {
+    cudaStream_t stream = nullptr;
+    uint8_t* slot[2] = {nullptr, nullptr};
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    cudaEvent_t done = nullptr;
+    int turn = 0;
+    double memcpy_seconds = 0, wait_seconds = 0;
+  };
+
+  cudaError_t ensure_workers(size_t n) {
+    while (workers_.size() < n) {
+      workers_.emplace_back();
+      Worker& w = workers_.back();
+      cudaError_t e = cudaStreamCreateWithFlags(&w.stream, cudaStreamNonBlocking);
+      for (int k = 0; k < 2 && e == cudaSuccess; ++k) {
+        e = cudaHostAlloc((void**)&w.slot[k], kSlotBytes, cudaHostAllocDefault);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&w.ev[k], cudaEventDisableTiming);
+      }
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&w.done, cudaEventDisableTiming);
+      if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+  }
+
+  int device_;
+  int nworkers_;
+  size_t used_ = 0;
+  std::vector<Worker> workers_;
+};
+
+// The device work of one batch: its packets, 64 KiB block jobs and A uploads.
+struct BatchInput {
+  size_t first = 0, last = 0;
+  std::vector<BlockJob> blocks;
+  std::vector<uint32_t> packet_first_block;
+  std::vector<Uploader::Piece> pieces;
+};
+
 }  // namespace
+
+bool alloc_host_chunk(uint64_t bytes, bool pinned, int threads, ArenaChunk* out, std::string* err) {
+  constexpr uint64_t kHuge = 2ull << 20;
+  const uint64_t size = (std::max<uint64_t>(bytes, 1) + kHuge - 1) & ~(kHuge - 1);
+  void* p = nullptr;
+  if (posix_memalign(&p, kHuge, size) != 0) {
+    *err = "cannot allocate " + std::to_string(bytes) + " bytes of host memory for the delta arena";
+    return false;
+  }
+  *out = ArenaChunk{(uint8_t*)p, 0, bytes, false};
+  if (!pinned) return true;
+  madvise(p, size, MADV_HUGEPAGE);  // advisory: fewer, larger pages to fault and lock
+  const int nt = (int)std::max<uint64_t>(1, std::min<uint64_t>((uint64_t)std::max(1, std::min(threads, 8)), size / (8ull << 20)));
+  const uint64_t per = (size / nt + kHuge - 1) & ~(kHuge - 1);
+  std::vector<std::thread> pool;
+  for (int t = 1; t < nt; ++t)
+    pool.emplace_back([=] {
+      const uint64_t a = std::min(size, t * per), b = std::min(size, a + per);
+      memset((uint8_t*)p + a, 0, b - a);
+    });
+  memset(p, 0, std::min(size, per));
+  for (auto& t : pool) t.join();
+  const cudaError_t e = cudaHostRegister(p, size, cudaHostRegisterPortable);
+  if (e != cudaSuccess) {
+    free(p);
+    *err = std::string("cannot page-lock the delta arena: ") + cudaGetErrorString(e);
+    return false;
+  }
+  out->pinned = true;
+  return true;
+}
+
+void free_host_chunk(const ArenaChunk& c) {
+  if (!c.ptr) return;
+  if (c.pinned) cudaHostUnregister(c.ptr);
+  free(c.ptr);
+}
 
 #define WS_GPU_TRY(expr)                                                             \
   do {                                                                               \
@@ -416,8 +614,20 @@ void fill_enc_table(const CodingTables& ct, EncTable* t) {
   } while (0)
 
 bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, int dict_slack_pct,
-                        uint64_t batch_bytes, cudaStream_t stream, std::vector<EncodedPacket>* out, std::string* err) {
+                        uint64_t batch_bytes, int threads, bool pin, cudaStream_t stream,
+                        std::vector<EncodedPacket>* out, std::vector<ArenaChunk>* chunks, std::string* err) {
   out->resize(packets.size());
+  int device = 0;
+  WS_GPU_TRY(cudaGetDevice(&device));
+  Uploader uploader(device, threads);
+  uint64_t arena_off = 0;
+  // WS_ENCODER_TIMING=1 prints the time spent in each phase to stderr.
+  const bool timing = getenv("WS_ENCODER_TIMING") != nullptr;
+  double t_upload = 0, t_stats = 0, t_tables = 0, t_encode = 0, t_pack = 0, t_alloc = 0, t_rule = 0;
+  auto now = [] { return std::chrono::steady_clock::now(); };
+  auto secs = [](std::chrono::steady_clock::time_point a, std::chrono::steady_clock::time_point b) {
+    return std::chrono::duration<double>(b - a).count();
+  };
   DeviceBuffer<uint8_t> d_base, d_payload, d_index;
   DeviceBuffer<BlockJob> d_blocks;
   DeviceBuffer<PacketStats> d_pstats;
@@ -429,28 +639,63 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
   DeviceBuffer<uint32_t> d_nwords;
   DeviceBuffer<CompactJob> d_compact;
   DeviceBuffer<uint16_t> d_words;
-  size_t first = 0;
-  while (first < packets.size()) {
-    // One batch: consecutive packets up to batch_bytes of weights.
+  // Batches: consecutive packets up to batch_bytes of weights; packets start
+  // 256-byte aligned in the device copy of A.
+  std::vector<std::pair<size_t, size_t>> ranges;
+  uint64_t max_bytes = 0;
+  for (size_t first = 0; first < packets.size();) {
     size_t last = first;
     uint64_t bytes = 0;
     while (last < packets.size() && (last == first || bytes + packets[last].nbytes <= batch_bytes))
-      bytes += (packets[last++].nbytes + 255) & ~255ull;  // packets start 256-byte aligned in the device copy
-    const size_t np = last - first;
-    WS_GPU_TRY(d_base.ensure(bytes));
-    std::vector<BlockJob> blocks;
-    std::vector<uint32_t> packet_first_block(np + 1);
+      bytes += (packets[last++].nbytes + 255) & ~255ull;
+    ranges.emplace_back(first, last);
+    max_bytes = std::max(max_bytes, bytes);
+    first = last;
+  }
+  if (ranges.empty()) return true;
+  // One device copy of A per batch. (Uploading batch k+1 on a helper thread
+  // while batch k is encoded was measured slower: the staging copies and the
+  // arena's page faults and page locking contend for the host.)
+  WS_GPU_TRY(d_base.ensure(max_bytes));
+  struct Event {
+    cudaEvent_t e = nullptr;  // the work reading d_base is done
+    ~Event() {
+      if (e) cudaEventDestroy(e);
+    }
+  } released;
+  WS_GPU_TRY(cudaEventCreateWithFlags(&released.e, cudaEventDisableTiming));
+  auto make_input = [&](size_t k, uint8_t* dbase) {
+    BatchInput in;
+    in.first = ranges[k].first;
+    in.last = ranges[k].second;
+    const size_t np = in.last - in.first;
+    in.packet_first_block.resize(np + 1);
     uint64_t off = 0;
     for (size_t i = 0; i < np; ++i) {
-      const GpuPacketInput& p = packets[first + i];
-      WS_GPU_TRY(cudaMemcpyAsync(d_base.ptr + off, p.base, p.nbytes, cudaMemcpyHostToDevice, stream));
-      packet_first_block[i] = (uint32_t)blocks.size();
+      const GpuPacketInput& p = packets[in.first + i];
+      if (p.nbytes) in.pieces.push_back(Uploader::Piece{dbase + off, p.base, p.nbytes});
+      in.packet_first_block[i] = (uint32_t)in.blocks.size();
       for (uint64_t b = 0; b < p.nbytes; b += WS_BLOCK_BYTES)
-        blocks.push_back(BlockJob{d_base.ptr + off + b, p.target + b,
-                                  (uint32_t)std::min<uint64_t>(WS_BLOCK_BYTES, p.nbytes - b), (uint32_t)i});
+        in.blocks.push_back(BlockJob{dbase + off + b, p.target + b,
+                                     (uint32_t)std::min<uint64_t>(WS_BLOCK_BYTES, p.nbytes - b), (uint32_t)i});
       off += (p.nbytes + 255) & ~255ull;
     }
-    packet_first_block[np] = (uint32_t)blocks.size();
+    in.packet_first_block[np] = (uint32_t)in.blocks.size();
+    return in;
+  };
+  for (size_t k = 0; k < ranges.size(); ++k) {
+    const BatchInput cur = make_input(k, d_base.ptr);
+    const auto t_up = now();
+    WS_GPU_TRY(cudaEventRecord(released.e, stream));
+    WS_GPU_TRY(uploader.copy(cur.pieces, released.e));
+    WS_GPU_TRY(uploader.order_before(stream));
+    if (timing) WS_GPU_TRY(cudaStreamSynchronize(stream));
+    t_upload += secs(t_up, now());
+    const size_t first = cur.first, last = cur.last;
+    const size_t np = last - first;
+    const std::vector<BlockJob>& blocks = cur.blocks;
+    const std::vector<uint32_t>& packet_first_block = cur.packet_first_block;
+    auto t0 = now();
     const size_t nb = blocks.size();
     WS_GPU_TRY(d_blocks.ensure(nb));
     WS_GPU_TRY(d_pstats.ensure(np));
@@ -466,6 +711,8 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
     WS_GPU_TRY(cudaMemcpyAsync(pstats.data(), d_pstats.ptr, np * sizeof(PacketStats), cudaMemcpyDeviceToHost, stream));
     WS_GPU_TRY(cudaMemcpyAsync(bstats.data(), d_bstats.ptr, nb * sizeof(BlockStats), cudaMemcpyDeviceToHost, stream));
     WS_GPU_TRY(cudaStreamSynchronize(stream));
+    t_stats += secs(t0, now());
+    t0 = now();
 
     // Tables per packet and candidate (host, shared code with the host encoder).
     struct Cand {
@@ -540,6 +787,8 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
         }
       }
     }
+    t_tables += secs(t0, now());
+    t0 = now();
     // Encode every candidate block.
     std::vector<uint32_t> nwords(jobs.size());
     if (!jobs.empty()) {
@@ -570,12 +819,10 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
       WS_GPU_TRY(cudaMemcpyAsync(nwords.data(), d_nwords.ptr, jobs.size() * 4, cudaMemcpyDeviceToHost, stream));
       WS_GPU_TRY(cudaStreamSynchronize(stream));
     }
+    t_encode += secs(t0, now());
+    t0 = now();
     // Mode rule (delta.py:184-193) and raw fallback, then pack the chosen payloads.
     std::vector<CompactJob> compact;
-    struct Pending {
-      size_t packet, block_index;
-    };
-    std::vector<Pending> pending;
     uint64_t out_bytes = 0;
     for (size_t i = 0; i < np; ++i) {
       EncodedPacket& e = (*out)[first + i];
@@ -636,28 +883,40 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
           }
         }
         ++jpos;
-        blk.payload.assign(size, 0);
+        blk.clen = size;
         compact.push_back(cj);
-        pending.push_back(Pending{first + i, e.blocks.size()});
         out_bytes += size;
         e.blocks.push_back(std::move(blk));
       }
     }
+    t_rule += secs(t0, now());
     if (!compact.empty()) {
       WS_GPU_TRY(d_compact.ensure(compact.size()));
       WS_GPU_TRY(d_payload.ensure(out_bytes));
       WS_GPU_TRY(cudaMemcpyAsync(d_compact.ptr, compact.data(), compact.size() * sizeof(CompactJob), cudaMemcpyHostToDevice, stream));
       compact_kernel<<<(unsigned)compact.size(), 256, 0, stream>>>(d_compact.ptr, d_blocks.ptr, d_enc.ptr, d_payload.ptr);
       WS_GPU_TRY(cudaGetLastError());
-      std::vector<uint8_t> host(out_bytes);
-      WS_GPU_TRY(cudaMemcpyAsync(host.data(), d_payload.ptr, out_bytes, cudaMemcpyDeviceToHost, stream));
-      WS_GPU_TRY(cudaStreamSynchronize(stream));
-      for (size_t k = 0; k < compact.size(); ++k) {
-        EncodedBlock& blk = (*out)[pending[k].packet].blocks[pending[k].block_index];
-        memcpy(blk.payload.data(), host.data() + compact[k].dst, blk.payload.size());
-      }
+      // The batch's payloads become one arena chunk (arena order is packet, block order).
+      ArenaChunk ch;
+      const auto ta = now();
+      if (!alloc_host_chunk(out_bytes, pin, threads, &ch, err)) return false;
+      t_alloc += secs(ta, now());
+      ch.off = arena_off;
+      chunks->push_back(ch);
+      WS_GPU_TRY(cudaMemcpyAsync(ch.ptr, d_payload.ptr, out_bytes, cudaMemcpyDeviceToHost, stream));
+      arena_off += out_bytes;
     }
-    first = last;
+    if (timing) WS_GPU_TRY(cudaStreamSynchronize(stream));
+    t_pack += secs(t0, now());
+  }
+  WS_GPU_TRY(cudaStreamSynchronize(stream));
+  if (timing) {
+    double mc = 0, wt = 0;
+    uploader.busy(&mc, &wt);
+    fprintf(stderr,
+            "gpu encoder: upload %.3f s (slot memcpy %.3f, slot wait %.3f thread-s), stats %.3f s, tables %.3f s, "
+            "encode %.3f s, pack %.3f s (mode rule %.3f, chunk allocation %.3f)\n",
+            t_upload, mc, wt, t_stats, t_tables, t_encode, t_pack, t_rule, t_alloc);
   }
   return true;
 }

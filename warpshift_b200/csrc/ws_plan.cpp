@@ -46,6 +46,7 @@ int fail(int code, const std::string& msg) {
 struct Batch {
   uint32_t tile_begin, tile_end;
   uint64_t arena_off, bytes;
+  uint32_t chunk;  // arena chunk holding the whole batch
 };
 
 struct PacketRef {
@@ -87,9 +88,9 @@ struct ws_plan {
   std::vector<ws_tile_desc> tiles;
   std::vector<uint32_t> tables;
   std::vector<Batch> batches;
-  uint8_t* arena = nullptr;
+  std::vector<ws::ArenaChunk> chunks;  // host arena: every block payload in block order
   uint64_t arena_bytes = 0;
-  bool arena_pinned = false;
+  uint8_t* view_arena = nullptr;       // contiguous copy made by ws_plan_get_view for a multi-chunk arena
   ws_plan_stats stats{};
 
   bool uploaded = false;
@@ -143,21 +144,24 @@ void release_device(ws_plan* p) {
   if (prev >= 0) cudaSetDevice(prev);
 }
 
+void free_chunks(std::vector<ws::ArenaChunk>* chunks) {
+  for (const ws::ArenaChunk& c : *chunks) ws::free_host_chunk(c);
+  chunks->clear();
+}
+
 void release_host(ws_plan* p) {
-  if (p->arena) {
-    if (p->arena_pinned)
-      cudaFreeHost(p->arena);
-    else
-      free(p->arena);
-  }
-  p->arena = nullptr;
+  free_chunks(&p->chunks);
+  free(p->view_arena);
+  p->view_arena = nullptr;
 }
 
 // Encode all packets. Device targets go through a ring of pinned staging
 // buffers: the calling thread issues D2H copies in packet order, workers wait
 // on each copy's event and encode.
 int encode_all(const ws_tensor_desc* tensors, const std::vector<PacketRef>& packets, const ws_build_options& o,
-               cudaStream_t stream, std::vector<ws::EncodedPacket>* out) {
+               cudaStream_t stream, std::vector<ws::EncodedPacket>* out, std::vector<ws::ArenaChunk>* chunks,
+               bool* external) {
+  *external = false;
   const int threads = o.threads > 0 ? o.threads : default_threads();
   out->resize(packets.size());
   if (o.target_on_device && o.encode_on_device) {
@@ -169,7 +173,10 @@ int encode_all(const ws_tensor_desc* tensors, const std::vector<PacketRef>& pack
                                       pr.nbytes, t.is_bf16 != 0});
     }
     std::string err;
-    if (!ws::gpu_encode_packets(in, o.policy, o.dict_slack_pct, 512ull << 20, stream, out, &err))
+    *external = true;
+    const uint64_t batch = o.encode_batch_bytes ? o.encode_batch_bytes : (512ull << 20);
+    if (!ws::gpu_encode_packets(in, o.policy, o.dict_slack_pct, batch, threads, o.pin_arena != 0, stream, out,
+                                chunks, &err))
       return fail(WS_ERR_CUDA, err);
     return WS_OK;
   }
@@ -267,8 +274,11 @@ int encode_all(const ws_tensor_desc* tensors, const std::vector<PacketRef>& pack
   return rc;
 }
 
+// Descriptors, tiles, staging batches and the host arena. With `external` the
+// payloads are already in p->chunks (GPU encoder); otherwise they are copied
+// from the encoded blocks into one chunk.
 int layout(ws_plan* p, const ws_tensor_desc* tensors, const std::vector<PacketRef>& packets,
-           std::vector<ws::EncodedPacket>& enc) {
+           std::vector<ws::EncodedPacket>& enc, bool external) {
   ws_plan_stats& st = p->stats;
   std::vector<uint64_t> packet_first_block(enc.size());
   uint64_t arena = 0;
@@ -304,7 +314,7 @@ int layout(ws_plan* p, const ws_tensor_desc* tensors, const std::vector<PacketRe
       d.dst = base_addr + b.offset;
       d.src = arena;
       d.nbytes = b.nbytes;
-      d.clen = (uint32_t)b.payload.size();
+      d.clen = external ? b.clen : (uint32_t)b.payload.size();
       d.nwords = b.nwords;
       d.kind = b.kind;
       d.tail = b.tail;
@@ -314,51 +324,61 @@ int layout(ws_plan* p, const ws_tensor_desc* tensors, const std::vector<PacketRe
       st.expected_checksum[1] += ws_block_hash(b.lane_sum[1], index);
       st.touched_bytes += b.nbytes;
       p->blocks.push_back(d);
-      arena += b.payload.size();
+      arena += d.clen;
     }
   }
+  if (!external) {  // one chunk holding every payload
+    if (arena) {
+      const int threads = p->opts.threads > 0 ? p->opts.threads : default_threads();
+      ws::ArenaChunk c;
+      std::string err;
+      if (!ws::alloc_host_chunk(arena, p->opts.pin_arena != 0, threads, &c, &err)) return fail(WS_ERR_NOMEM, err);
+      p->chunks.push_back(c);
+      parallel_for(enc.size(), threads, [&](uint64_t i) {
+        if (enc[i].mode == WS_MODE_SKIP) return;
+        uint64_t first = packet_first_block[i];
+        for (size_t k = 0; k < enc[i].blocks.size(); ++k) {
+          const auto& pl = enc[i].blocks[k].payload;
+          memcpy(c.ptr + p->blocks[first + k].src, pl.data(), pl.size());
+        }
+      });
+    }
+  } else {
+    uint64_t covered = 0;
+    for (const ws::ArenaChunk& c : p->chunks) {
+      if (c.off != covered) return fail(WS_ERR_STATE, "internal: arena chunks are not contiguous");
+      covered += c.bytes;
+    }
+    if (covered != arena) return fail(WS_ERR_STATE, "internal: arena chunks do not match the block layout");
+  }
   if (p->blocks.size() > 0xFFFFFFFFull) return fail(WS_ERR_INVALID, "too many blocks in one plan");
-  // Batches: contiguous tile ranges whose payload fits one staging slot.
+  // Batches: contiguous tile ranges of one arena chunk whose payload fits one
+  // staging slot. A tile never spans chunks (chunks end at packet boundaries).
   const uint64_t limit = p->opts.batch_bytes;
-  Batch cur{0, 0, 0, 0};
+  Batch cur{0, 0, 0, 0, 0};
   bool open = false;
+  uint32_t chunk = 0;
   for (uint32_t t = 0; t < p->tiles.size(); ++t) {
     const ws_tile_desc& td = p->tiles[t];
     const ws_block_desc& first = p->blocks[td.first_block];
     const ws_block_desc& last = p->blocks[td.first_block + td.nblocks - 1];
     const uint64_t bytes = last.src + last.clen - first.src;  // tiles are contiguous in the arena
-    if (open && cur.bytes + bytes > limit) {
+    while (chunk < p->chunks.size() && first.src >= p->chunks[chunk].off + p->chunks[chunk].bytes) ++chunk;
+    if (chunk >= p->chunks.size() || last.src + last.clen > p->chunks[chunk].off + p->chunks[chunk].bytes)
+      return fail(WS_ERR_STATE, "internal: a tile spans two arena chunks");
+    if (open && (cur.bytes + bytes > limit || cur.chunk != chunk)) {
       p->batches.push_back(cur);
       open = false;
     }
     if (!open) {
-      cur = Batch{t, t, first.src, 0};
+      cur = Batch{t, t, first.src, 0, chunk};
       open = true;
     }
     cur.tile_end = t + 1;
     cur.bytes += bytes;
   }
   if (open) p->batches.push_back(cur);
-  // Arena: every payload, in block order.
   p->arena_bytes = arena;
-  if (arena) {
-    if (p->opts.pin_arena) {
-      if (cudaHostAlloc((void**)&p->arena, arena, cudaHostAllocDefault) != cudaSuccess)
-        return fail(WS_ERR_NOMEM, "cannot allocate the pinned delta arena");
-      p->arena_pinned = true;
-    } else {
-      if (posix_memalign((void**)&p->arena, 4096, arena) != 0) return fail(WS_ERR_NOMEM, "cannot allocate arena");
-    }
-    const int threads = p->opts.threads > 0 ? p->opts.threads : default_threads();
-    parallel_for(enc.size(), threads, [&](uint64_t i) {
-      if (enc[i].mode == WS_MODE_SKIP) return;
-      uint64_t first = packet_first_block[i];
-      for (size_t k = 0; k < enc[i].blocks.size(); ++k) {
-        const auto& pl = enc[i].blocks[k].payload;
-        memcpy(p->arena + p->blocks[first + k].src, pl.data(), pl.size());
-      }
-    });
-  }
   st.arena_bytes = arena;
   st.table_bytes = p->tables.size() * 4;
   st.metadata_bytes = p->blocks.size() * sizeof(ws_block_desc) + p->tiles.size() * sizeof(ws_tile_desc) +
@@ -436,8 +456,15 @@ int ws_plan_build(const ws_tensor_desc* tensors, uint64_t ntensors, const ws_bui
     }
   }
   std::vector<ws::EncodedPacket> enc;
-  int rc = encode_all(tensors, packets, p->opts, (cudaStream_t)stream, &enc);
-  if (rc == WS_OK) rc = layout(p, tensors, packets, enc);
+  bool external = false;
+  const auto t_enc = std::chrono::steady_clock::now();
+  int rc = encode_all(tensors, packets, p->opts, (cudaStream_t)stream, &enc, &p->chunks, &external);
+  const auto t_lay = std::chrono::steady_clock::now();
+  if (rc == WS_OK) rc = layout(p, tensors, packets, enc, external);
+  if (getenv("WS_ENCODER_TIMING"))
+    fprintf(stderr, "plan build: encode %.3f s, layout %.3f s\n",
+            std::chrono::duration<double>(t_lay - t_enc).count(),
+            std::chrono::duration<double>(std::chrono::steady_clock::now() - t_lay).count());
   if (prev >= 0) cudaSetDevice(prev);
   if (rc != WS_OK) {
     release_host(p);
@@ -507,8 +534,9 @@ int ws_plan_set_resident(ws_plan* p, int resident, void* stream) {
   WS_CUDA_TRY(cudaSetDevice(p->device));
   if (resident && !p->d_resident && p->arena_bytes) {
     cudaError_t e = cudaMalloc((void**)&p->d_resident, p->arena_bytes);
-    if (e == cudaSuccess)
-      e = cudaMemcpyAsync(p->d_resident, p->arena, p->arena_bytes, cudaMemcpyHostToDevice, (cudaStream_t)stream);
+    for (size_t c = 0; c < p->chunks.size() && e == cudaSuccess; ++c)
+      e = cudaMemcpyAsync(p->d_resident + p->chunks[c].off, p->chunks[c].ptr, p->chunks[c].bytes,
+                          cudaMemcpyHostToDevice, (cudaStream_t)stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
     if (e != cudaSuccess) {
       cudaFree(p->d_resident);
@@ -552,7 +580,9 @@ int ws_apply_async(ws_plan* p, int reverse, void* compute_stream, void* copy_str
       const Batch& bt = p->batches[b];
       const size_t slot = b % nslots;
       if (b >= nslots) WS_CUDA_TRY(cudaStreamWaitEvent(copy, p->compute_done[slot], 0));
-      WS_CUDA_TRY(cudaMemcpyAsync(p->d_slots[slot], p->arena + bt.arena_off, bt.bytes, cudaMemcpyHostToDevice, copy));
+      const ws::ArenaChunk& ch = p->chunks[bt.chunk];
+      WS_CUDA_TRY(cudaMemcpyAsync(p->d_slots[slot], ch.ptr + (bt.arena_off - ch.off), bt.bytes,
+                                  cudaMemcpyHostToDevice, copy));
       WS_CUDA_TRY(cudaEventRecord(p->copy_done[slot], copy));
       WS_CUDA_TRY(cudaStreamWaitEvent(comp, p->copy_done[slot], 0));
       WS_CUDA_TRY(ws::launch_apply(p->d_tiles, bt.tile_begin, bt.tile_end - bt.tile_begin, p->d_blocks, p->d_tables,
@@ -620,13 +650,25 @@ int ws_plan_get_stats(const ws_plan* p, ws_plan_stats* out) {
 
 int ws_plan_get_view(const ws_plan* p, ws_plan_view* out) {
   if (!p || !out) return fail(WS_ERR_INVALID, "null argument");
+  const uint8_t* arena = p->chunks.empty() ? nullptr : p->chunks[0].ptr;
+  if (p->chunks.size() > 1) {  // one contiguous host copy, made once
+    ws_plan* mp = const_cast<ws_plan*>(p);
+    if (!mp->view_arena) {
+      if (posix_memalign((void**)&mp->view_arena, 4096, p->arena_bytes) != 0) {
+        mp->view_arena = nullptr;
+        return fail(WS_ERR_NOMEM, "cannot allocate the contiguous arena view");
+      }
+      for (const ws::ArenaChunk& c : p->chunks) memcpy(mp->view_arena + c.off, c.ptr, c.bytes);
+    }
+    arena = mp->view_arena;
+  }
   out->blocks = p->blocks.data();
   out->nblocks = p->blocks.size();
   out->tiles = p->tiles.data();
   out->ntiles = p->tiles.size();
   out->tables = p->tables.data();
   out->ntables = p->tables.size() / 512;
-  out->arena = p->arena;
+  out->arena = arena;
   out->arena_bytes = p->arena_bytes;
   return WS_OK;
 }
