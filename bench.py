@@ -490,7 +490,19 @@ def run_ours(args) -> None:
         if entry:
             traffic = entry["dram_bytes_per_launch"]
     t_roof_ms = max(C / (h2d_gbs * 1e9) if h2d_gbs == h2d_gbs else 0.0, algo_bytes / (pk["hbm_gbs"] * 1e9)) * 1e3
-    # Exactness check of the final state against a regenerated Teacher (first and last tensor).
+    # On-device per-tensor hashes of the switched weights (the replacement for the
+    # acceptance check's D2H sha256), timed over every tensor of this rank.
+    from warpshift_b200.verify import tensor_hashes
+
+    tensor_hashes(gpu)
+    hs, he = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    hs.record()
+    final_hashes = tensor_hashes(gpu)
+    he.record()
+    torch.cuda.synchronize(device)
+    hash_ms = hs.elapsed_time(he)
+    # Exactness check of the final state against a regenerated Teacher (first and
+    # last tensor): bytes and device hashes.
     from warpshift_b200 import synth
 
     for i in (0, len(spec.tensors) - 1):
@@ -500,6 +512,8 @@ def run_ours(args) -> None:
             synth.perturb_(ref, t, i, args.scale)
         if not torch.equal(ref.reshape(-1).view(torch.uint8), gpu[t.name].reshape(-1).view(torch.uint8)):
             raise RuntimeError(f"final weights differ from the regenerated teacher on {t.name}")
+        if tensor_hashes({t.name: ref})[t.name] != final_hashes[t.name]:
+            raise RuntimeError(f"device hash of {t.name} differs from the regenerated teacher's")
     if rank != 0:
         return
     line = {
@@ -552,6 +566,13 @@ def run_ours(args) -> None:
             "kernel": "ws_apply_kernel (fused rANS decode + in-place apply)",
         },
         "full_copy": full_copy,
+        "tensor_hash": {
+            "ms": round(hash_ms, 3),
+            "gbs": round(W / (hash_ms * 1e-3) / 1e9, 1),
+            "frac_of_hbm_peak": round(W / (hash_ms * 1e-3) / 1e9 / pk["hbm_gbs"], 3),
+            "tensors": len(final_hashes),
+            "path": "warpshift_b200.verify.tensor_hashes (ws_tensor_hashes), all tensors of the rank, one call",
+        },
         "gpu_launches": launches_k + launches_e,
         "clocks": clocks,
     }

@@ -174,6 +174,17 @@ WS_API int ws_plan_get_view(const ws_plan* plan, ws_plan_view* out);
 WS_API int ws_apply_device_noalloc(const void* tiles, uint32_t ntiles, const void* blocks, const uint32_t* tables,
                                    const void* payload, int reverse, int device, void* stream, ws_apply_result* out);
 
+/* No counterpart in the reference's API: replaces the acceptance check's per-tensor
+ * sha256 (scripts/validate.py:50-56: D2H in 64 MiB pieces, hashed on the host)
+ * with one pass over the resident bytes on `device`. out[i] = 64-bit hash of the
+ * nbytes[i] bytes at ptrs[i] (device memory, any alignment): with w_j the
+ * little-endian 64-bit words (last one zero-padded),
+ *   hash = mix64(sum_j mix64(w_j ^ (j + 1) * 0xC2B2AE3D27D4EB4F) + (nbytes + 1) * 0x165667B19E3779F9)
+ * (arithmetic mod 2^64, mix64 = the splitmix64 finaliser). Allocates two small
+ * stream-ordered device buffers; returns after `stream` completes. */
+WS_API int ws_tensor_hashes(const void* const* ptrs, const uint64_t* nbytes, uint64_t n, int device, void* stream,
+                            uint64_t* out);
+
 /* Frees host and device resources (delta.py relies on GC for the same). */
 WS_API void ws_plan_destroy(ws_plan* plan);
 

@@ -100,6 +100,7 @@ SIGNATURES = {
     "ws_plan_get_view": ([P, ctypes.POINTER(PlanView)], ctypes.c_int),
     "ws_plan_destroy": ([P], None),
     "ws_apply_device_noalloc": ([P, u32, P, P, P, ctypes.c_int, ctypes.c_int, P, ctypes.POINTER(ApplyResult)], ctypes.c_int),
+    "ws_tensor_hashes": ([ctypes.POINTER(P), ctypes.POINTER(u64), u64, ctypes.c_int, P, ctypes.POINTER(u64)], ctypes.c_int),
 }
 WS_NOALLOC_MAX_TILES = 16384
 

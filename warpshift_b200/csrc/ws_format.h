@@ -110,6 +110,9 @@ typedef struct ws_device_result {
 // mix64 is the splitmix64 finaliser (Steele, Lea, Flood 2014).
 #define WS_CK_K1 0x9E3779B97F4A7C15ull
 #define WS_CK_K2 0xD1B54A32D192ED03ull
+// Per-tensor content hash (ws_tensor_hashes): word position and length keys.
+#define WS_TH_KPOS 0xC2B2AE3D27D4EB4Full
+#define WS_TH_KLEN 0x165667B19E3779F9ull
 
 #ifdef __CUDACC__
 #define WS_HD __host__ __device__ __forceinline__

@@ -1,0 +1,156 @@
+// Per-tensor content hashes on the device (ws_tensor_hashes).
+//
+// Replaces the acceptance check's per-tensor sha256 (scripts/validate.py:50-56),
+// which copies every tensor to the host in 64 MiB pieces, with one HBM-bound
+// pass over the resident bytes. Definition (restated by the oracle): for a
+// tensor of N bytes, let w_i be its little-endian 64-bit words (the last one
+// zero-padded) and
+//   sum  = sum_i mix64(w_i ^ ((i + 1) * WS_TH_KPOS))   (mod 2^64)
+//   hash = mix64(sum + (N + 1) * WS_TH_KLEN)           (mod 2^64)
+// where mix64 is the splitmix64 finaliser. The terms are keyed by position and
+// summed, so any split of the words over warps gives the same value.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "../../include/warpshift_b200.h"
+#include "ws_format.h"
+
+namespace ws {
+void set_last_error(const char* msg);
+}
+
+namespace {
+
+constexpr uint32_t kSegWords = 8192;  // one warp hashes 64 KiB at a time
+constexpr uint32_t kHashThreads = 256;
+constexpr uint32_t kHashBlocksPerSm = 8;
+
+struct HashTensor {
+  const uint8_t* ptr;
+  uint64_t nbytes;
+  uint64_t first_seg;  // first 64 KiB segment of this tensor in the flattened list
+};
+
+__device__ __forceinline__ uint64_t term(uint64_t w, uint64_t i) { return ws_mix64(w ^ ((i + 1) * WS_TH_KPOS)); }
+
+// Word i assembled from bytes (unaligned bases and the zero-padded tail).
+__device__ __forceinline__ uint64_t word_bytes(const uint8_t* p, uint64_t nbytes, uint64_t i) {
+  uint64_t w = 0;
+  const uint64_t b0 = i * 8;
+#pragma unroll
+  for (uint32_t k = 0; k < 8; ++k)
+    if (b0 + k < nbytes) w |= (uint64_t)__ldg(p + b0 + k) << (8 * k);
+  return w;
+}
+
+__global__ void __launch_bounds__(kHashThreads)
+    ws_tensor_hash_kernel(const HashTensor* __restrict__ tensors, uint32_t n, uint64_t nseg,
+                          unsigned long long* __restrict__ acc) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint64_t warps = (uint64_t)gridDim.x * (kHashThreads / 32);
+  for (uint64_t seg = (uint64_t)blockIdx.x * (kHashThreads / 32) + (threadIdx.x >> 5); seg < nseg; seg += warps) {
+    // Owner: the last tensor whose first segment is <= seg (tensors are non-empty).
+    uint32_t lo = 0, hi = n;
+    while (hi - lo > 1) {
+      const uint32_t mid = (lo + hi) >> 1;
+      if (tensors[mid].first_seg <= seg) lo = mid; else hi = mid;
+    }
+    const HashTensor t = tensors[lo];
+    const uint64_t nwords = (t.nbytes + 7) / 8, full = t.nbytes / 8;
+    const uint64_t w0 = (seg - t.first_seg) * kSegWords;
+    const uint64_t w1 = min(w0 + kSegWords, nwords);
+    uint64_t sum = 0;
+    if (((uintptr_t)t.ptr & 15u) == 0) {
+      // Lane l hashes words (w, w + 1) for w = w0 + 2l + 64k: 16-byte loads, 512
+      // contiguous bytes per warp and step, four steps in flight.
+      const uint4* v = reinterpret_cast<const uint4*>(t.ptr);
+      uint64_t w = w0 + 2 * lane;
+      for (; w + 3 * 64 + 2 <= min(w1, full); w += 4 * 64) {
+        uint4 x[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) x[k] = __ldg(v + (w + 64 * k) / 2);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t i = w + 64 * k;
+          sum += term(((uint64_t)x[k].y << 32) | x[k].x, i) + term(((uint64_t)x[k].w << 32) | x[k].z, i + 1);
+        }
+      }
+      for (; w < w1; w += 64) {
+        if (w + 2 <= full) {
+          const uint4 x = __ldg(v + w / 2);
+          sum += term(((uint64_t)x.y << 32) | x.x, w) + term(((uint64_t)x.w << 32) | x.z, w + 1);
+        } else {
+          sum += term(word_bytes(t.ptr, t.nbytes, w), w);
+          if (w + 1 < w1) sum += term(word_bytes(t.ptr, t.nbytes, w + 1), w + 1);
+        }
+      }
+    } else {
+      for (uint64_t w = w0 + lane; w < w1; w += 32) sum += term(word_bytes(t.ptr, t.nbytes, w), w);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+    if (lane == 0) atomicAdd(acc + lo, (unsigned long long)sum);
+  }
+}
+
+int fail(int code, const std::string& msg) {
+  ws::set_last_error(msg.c_str());
+  return code;
+}
+
+}  // namespace
+
+extern "C" int ws_tensor_hashes(const void* const* ptrs, const uint64_t* nbytes, uint64_t n, int device, void* stream,
+                                uint64_t* out) {
+  if (n && (!ptrs || !nbytes || !out)) return fail(WS_ERR_INVALID, "null argument");
+  std::vector<HashTensor> list;
+  std::vector<uint64_t> owner;  // index into ptrs of each listed tensor
+  uint64_t nseg = 0;
+  for (uint64_t i = 0; i < n; ++i) {
+    if (nbytes[i] == 0) continue;
+    if (!ptrs[i]) return fail(WS_ERR_INVALID, "tensor " + std::to_string(i) + " has a null pointer");
+    list.push_back(HashTensor{(const uint8_t*)ptrs[i], nbytes[i], nseg});
+    owner.push_back(i);
+    nseg += ((nbytes[i] + 7) / 8 + kSegWords - 1) / kSegWords;
+  }
+  if (list.size() > 0xFFFFFFFFull) return fail(WS_ERR_INVALID, "too many tensors");
+  std::vector<unsigned long long> acc(list.size(), 0);
+  if (!list.empty()) {
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaError_t e = cudaSetDevice(device);
+    cudaStream_t s = (cudaStream_t)stream;
+    HashTensor* d_list = nullptr;
+    unsigned long long* d_acc = nullptr;
+    int sms = 0;
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (e == cudaSuccess) e = cudaMallocAsync((void**)&d_list, list.size() * sizeof(HashTensor), s);
+    if (e == cudaSuccess) e = cudaMallocAsync((void**)&d_acc, acc.size() * sizeof(unsigned long long), s);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(d_list, list.data(), list.size() * sizeof(HashTensor), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(d_acc, 0, acc.size() * sizeof(unsigned long long), s);
+    if (e == cudaSuccess) {
+      const uint64_t warps_needed = nseg;
+      const uint64_t blocks = std::min<uint64_t>((uint64_t)sms * kHashBlocksPerSm,
+                                                 (warps_needed + kHashThreads / 32 - 1) / (kHashThreads / 32));
+      ws_tensor_hash_kernel<<<(unsigned)blocks, kHashThreads, 0, s>>>(d_list, (uint32_t)list.size(), nseg, d_acc);
+      e = cudaGetLastError();
+    }
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(acc.data(), d_acc, acc.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost, s);
+    if (d_list) cudaFreeAsync(d_list, s);
+    if (d_acc) cudaFreeAsync(d_acc, s);
+    const cudaError_t es = cudaStreamSynchronize(s);
+    if (e == cudaSuccess) e = es;
+    if (prev >= 0) cudaSetDevice(prev);
+    if (e != cudaSuccess) return fail(WS_ERR_CUDA, std::string("tensor hashes: ") + cudaGetErrorString(e));
+  }
+  for (uint64_t i = 0; i < n; ++i) out[i] = ws_mix64((uint64_t)(nbytes[i] + 1) * WS_TH_KLEN);
+  for (size_t k = 0; k < list.size(); ++k)
+    out[owner[k]] = ws_mix64((uint64_t)acc[k] + (uint64_t)(nbytes[owner[k]] + 1) * WS_TH_KLEN);
+  return WS_OK;
+}
