@@ -36,6 +36,7 @@ extern "C" {
 #define WS_ERR_CHECKSUM 4 /* written bytes do not hash to the value recorded at prepare */
 #define WS_ERR_NOMEM 5    /* host or device allocation failed */
 #define WS_ERR_STATE 6    /* call out of order (e.g. apply before upload) */
+#define WS_ERR_IO 7       /* file cannot be created, written or read (saved plans) */
 
 #define WS_POLICY_AUTO 0 /* delta.py:176-194: raw XOR, else grouped/odd XOR-ANS, else U16-ANS if strictly smaller */
 #define WS_POLICY_XOR 1  /* only XOR representations (modes 0/1/2) */
@@ -173,6 +174,22 @@ WS_API int ws_plan_get_view(const ws_plan* plan, ws_plan_view* out);
 #define WS_NOALLOC_MAX_TILES 16384
 WS_API int ws_apply_device_noalloc(const void* tiles, uint32_t ntiles, const void* blocks, const uint32_t* tables,
                                    const void* payload, int reverse, int device, void* stream, ws_apply_result* out);
+
+/* No counterpart in the reference, which prepares the delta again after every
+ * restart (README.md:41). Writes a built plan to `path` (via `path`.tmp, then
+ * rename): descriptors with destinations stored as offsets inside their tensor,
+ * decode tables, tensor sizes, the expected checksums and the payload arena. */
+WS_API int ws_plan_save(const ws_plan* plan, const char* path);
+
+/* Re-creates a saved plan for `tensors`: the same count, byte sizes and BF16 flags
+ * in the same order as at build (`base` pointers are ignored; A is not needed).
+ * Block destinations are rebased onto the new targets; every descriptor is checked
+ * against the tensors and the arena, and the metadata against its stored hash.
+ * The arena is read into host memory (page-locked with opts->pin_arena) by up to
+ * opts->threads readers. Follow with ws_plan_upload as after ws_plan_build; the
+ * first apply's checksum confirms the resident weights were the expected source. */
+WS_API int ws_plan_load(const char* path, const ws_tensor_desc* tensors, uint64_t ntensors,
+                        const ws_build_options* opts, ws_plan** out);
 
 /* No counterpart in the reference's API: replaces the acceptance check's per-tensor
  * sha256 (scripts/validate.py:50-56: D2H in 64 MiB pieces, hashed on the host)

@@ -13,7 +13,7 @@ from pathlib import Path
 
 LIBRARY = Path(__file__).resolve().parent / "libwarpshift_b200.so"
 
-WS_OK, WS_ERR_INVALID, WS_ERR_CUDA, WS_ERR_DEVICE, WS_ERR_CHECKSUM, WS_ERR_NOMEM, WS_ERR_STATE = range(7)
+WS_OK, WS_ERR_INVALID, WS_ERR_CUDA, WS_ERR_DEVICE, WS_ERR_CHECKSUM, WS_ERR_NOMEM, WS_ERR_STATE, WS_ERR_IO = range(8)
 POLICIES = {"auto": 0, "xor": 1, "u16": 2}
 MODE_NAMES = ("XOR_RAW", "XOR_GROUP2_ANS", "XOR_ANS", "U16_ANS", "SKIP")
 
@@ -100,6 +100,8 @@ SIGNATURES = {
     "ws_plan_get_view": ([P, ctypes.POINTER(PlanView)], ctypes.c_int),
     "ws_plan_destroy": ([P], None),
     "ws_apply_device_noalloc": ([P, u32, P, P, P, ctypes.c_int, ctypes.c_int, P, ctypes.POINTER(ApplyResult)], ctypes.c_int),
+    "ws_plan_save": ([P, ctypes.c_char_p], ctypes.c_int),
+    "ws_plan_load": ([ctypes.c_char_p, ctypes.POINTER(TensorDesc), u64, ctypes.POINTER(BuildOptions), ctypes.POINTER(P)], ctypes.c_int),
     "ws_tensor_hashes": ([ctypes.POINTER(P), ctypes.POINTER(u64), u64, ctypes.c_int, P, ctypes.POINTER(u64)], ctypes.c_int),
 }
 WS_NOALLOC_MAX_TILES = 16384
@@ -140,4 +142,6 @@ def check(rc: int) -> None:
     message = last_error()
     if rc == WS_ERR_INVALID:
         raise ValueError(message)
+    if rc == WS_ERR_IO:
+        raise OSError(message)
     raise RuntimeError(message)

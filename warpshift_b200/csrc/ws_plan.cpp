@@ -27,8 +27,11 @@
 #include "ws_format.h"
 #include "ws_gpu_encoder.h"
 #include "ws_kernels.h"
+#include "ws_plan_internal.h"
 
 namespace {
+
+using ws::Batch;
 
 thread_local std::string g_last_error;
 
@@ -43,11 +46,6 @@ int fail(int code, const std::string& msg) {
     if (e_ != cudaSuccess) return fail(WS_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
   } while (0)
 
-struct Batch {
-  uint32_t tile_begin, tile_end;
-  uint64_t arena_off, bytes;
-  uint32_t chunk;  // arena chunk holding the whole batch
-};
 
 struct PacketRef {
   uint32_t tensor;
@@ -81,35 +79,6 @@ namespace ws {
 void set_last_error(const char* msg) { g_last_error = msg; }
 }  // namespace ws
 
-struct ws_plan {
-  ws_build_options opts{};
-  int device = -1;
-  std::vector<ws_block_desc> blocks;
-  std::vector<ws_tile_desc> tiles;
-  std::vector<uint32_t> tables;
-  std::vector<Batch> batches;
-  std::vector<ws::ArenaChunk> chunks;  // host arena: every block payload in block order
-  uint64_t arena_bytes = 0;
-  uint8_t* view_arena = nullptr;       // contiguous copy made by ws_plan_get_view for a multi-chunk arena
-  ws_plan_stats stats{};
-
-  bool uploaded = false;
-  ws_block_desc* d_blocks = nullptr;
-  ws_tile_desc* d_tiles = nullptr;
-  uint32_t* d_tables = nullptr;
-  std::vector<uint8_t*> d_slots;
-  uint64_t slot_bytes = 0;
-  uint8_t* d_resident = nullptr;
-  ws_device_result* d_result = nullptr;
-  ws_device_result* h_result = nullptr;
-  std::vector<cudaEvent_t> copy_done, compute_done;
-  cudaEvent_t start_event = nullptr;
-  cudaStream_t own_copy_stream = nullptr;
-
-  int pending_reverse = -1;
-  uint64_t pending_h2d = 0;
-  uint32_t pending_launches = 0;
-};
 
 namespace {
 
@@ -324,6 +293,7 @@ int layout(ws_plan* p, const ws_tensor_desc* tensors, const std::vector<PacketRe
       st.expected_checksum[1] += ws_block_hash(b.lane_sum[1], index);
       st.touched_bytes += b.nbytes;
       p->blocks.push_back(d);
+      p->block_tensor.push_back(pr.tensor);
       arena += d.clen;
     }
   }
@@ -352,6 +322,27 @@ int layout(ws_plan* p, const ws_tensor_desc* tensors, const std::vector<PacketRe
     if (covered != arena) return fail(WS_ERR_STATE, "internal: arena chunks do not match the block layout");
   }
   if (p->blocks.size() > 0xFFFFFFFFull) return fail(WS_ERR_INVALID, "too many blocks in one plan");
+  {
+    std::string err;
+    const int rc = ws::form_batches(p, &err);
+    if (rc != WS_OK) return fail(rc, err);
+  }
+  p->arena_bytes = arena;
+  st.arena_bytes = arena;
+  st.table_bytes = p->tables.size() * 4;
+  st.metadata_bytes = p->blocks.size() * sizeof(ws_block_desc) + p->tiles.size() * sizeof(ws_tile_desc) +
+                      st.table_bytes;
+  st.blocks = p->blocks.size();
+  st.tiles = p->tiles.size();
+  return WS_OK;
+}
+
+}  // namespace
+
+namespace ws {
+
+int form_batches(ws_plan* p, std::string* err) {
+  p->batches.clear();
   // Batches: contiguous tile ranges of one arena chunk whose payload fits one
   // staging slot. A tile never spans chunks (chunks end at packet boundaries).
   const uint64_t limit = p->opts.batch_bytes;
@@ -364,8 +355,10 @@ int layout(ws_plan* p, const ws_tensor_desc* tensors, const std::vector<PacketRe
     const ws_block_desc& last = p->blocks[td.first_block + td.nblocks - 1];
     const uint64_t bytes = last.src + last.clen - first.src;  // tiles are contiguous in the arena
     while (chunk < p->chunks.size() && first.src >= p->chunks[chunk].off + p->chunks[chunk].bytes) ++chunk;
-    if (chunk >= p->chunks.size() || last.src + last.clen > p->chunks[chunk].off + p->chunks[chunk].bytes)
-      return fail(WS_ERR_STATE, "internal: a tile spans two arena chunks");
+    if (chunk >= p->chunks.size() || last.src + last.clen > p->chunks[chunk].off + p->chunks[chunk].bytes) {
+      *err = "internal: a tile spans two arena chunks";
+      return WS_ERR_STATE;
+    }
     if (open && (cur.bytes + bytes > limit || cur.chunk != chunk)) {
       p->batches.push_back(cur);
       open = false;
@@ -378,18 +371,18 @@ int layout(ws_plan* p, const ws_tensor_desc* tensors, const std::vector<PacketRe
     cur.bytes += bytes;
   }
   if (open) p->batches.push_back(cur);
-  p->arena_bytes = arena;
-  st.arena_bytes = arena;
-  st.table_bytes = p->tables.size() * 4;
-  st.metadata_bytes = p->blocks.size() * sizeof(ws_block_desc) + p->tiles.size() * sizeof(ws_tile_desc) +
-                      st.table_bytes;
-  st.blocks = p->blocks.size();
-  st.tiles = p->tiles.size();
-  st.batches = p->batches.size();
+  p->stats.batches = p->batches.size();
   return WS_OK;
 }
 
-}  // namespace
+void free_plan_resources(ws_plan* p) {
+  release_device(p);
+  release_host(p);
+}
+
+int host_threads(int requested) { return requested > 0 ? requested : default_threads(); }
+
+}  // namespace ws
 
 extern "C" {
 
@@ -446,7 +439,12 @@ int ws_plan_build(const ws_tensor_desc* tensors, uint64_t ntensors, const ws_bui
   for (uint64_t i = 0; i < ntensors; ++i)
     for (uint64_t off = 0; off < tensors[i].nbytes; off += WS_PACKET_BYTES)
       packets.push_back(PacketRef{(uint32_t)i, off, std::min<uint64_t>(WS_PACKET_BYTES, tensors[i].nbytes - off)});
-  for (uint64_t i = 0; i < ntensors; ++i) p->stats.runtime_bytes += tensors[i].nbytes;
+  for (uint64_t i = 0; i < ntensors; ++i) {
+    p->stats.runtime_bytes += tensors[i].nbytes;
+    p->tensor_bytes.push_back(tensors[i].nbytes);
+    p->tensor_bf16.push_back(tensors[i].is_bf16 ? 1 : 0);
+    p->tensor_target.push_back((uint64_t)(uintptr_t)tensors[i].target);
+  }
   int prev = -1;
   if (opts->target_on_device) {
     cudaGetDevice(&prev);
@@ -675,8 +673,7 @@ int ws_plan_get_view(const ws_plan* p, ws_plan_view* out) {
 
 void ws_plan_destroy(ws_plan* p) {
   if (!p) return;
-  release_device(p);
-  release_host(p);
+  ws::free_plan_resources(p);
   delete p;
 }
 

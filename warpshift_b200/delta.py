@@ -16,6 +16,7 @@ set, which the XOR-only and U16-only benchmark configurations need.
 from __future__ import annotations
 
 import ctypes
+import os
 import time
 from typing import Any
 
@@ -127,7 +128,58 @@ class DeltaWeights:
             stream = self.compute_stream.cuda_stream
             _lib.check(self._native.ws_plan_build(descs, len(gpu_target), ctypes.byref(options), stream, ctypes.byref(plan)))
             self._plan = plan
-            _lib.check(self._native.ws_plan_upload(plan, stream))
+        self._finish(started, batch_bytes, "gpu" if encode_on_device else "host", dict_slack_pct)
+
+    @classmethod
+    def load(
+        cls,
+        path: str | os.PathLike,
+        gpu_target: dict[str, torch.Tensor],
+        *,
+        threads: int = 0,
+        batch_bytes: int = _STAGING_BATCH_BYTES,
+        staging_slots: int = 3,
+    ) -> "DeltaWeights":
+        """Re-create a package written by ``save`` for ``gpu_target`` (no prepare, no A).
+
+        ``gpu_target`` must hold the same tensors (names in the same order, same
+        shapes and dtypes) as when the package was built; its storage may live at
+        new addresses. The first ``apply`` checks, through the checksum recorded at
+        prepare, that the resident weights are the expected source model. Raises
+        ``ValueError`` if the file does not match the tensors and ``OSError`` if it
+        cannot be read.
+        """
+        started = time.perf_counter()
+        self = cls.__new__(cls)
+        self._plan = None
+        self._bind_targets(gpu_target)
+        self._native = _lib.load()
+        self.policy = "saved"
+        self.compute_stream = torch.cuda.current_stream(self.device)
+        self.copy_stream = torch.cuda.Stream(device=self.device)
+        descs = (_lib.TensorDesc * len(gpu_target))()
+        for index, target in enumerate(gpu_target.values()):
+            descs[index] = _lib.TensorDesc(
+                None, target.data_ptr(), target.numel() * target.element_size(), int(target.dtype == torch.bfloat16), 0
+            )
+        options = _lib.BuildOptions(
+            policy=0, threads=threads, target_on_device=1, device=self.device.index, batch_bytes=batch_bytes,
+            staging_slots=staging_slots, pin_arena=1, dict_slack_pct=_DICT_SLACK_PCT, encode_on_device=0,
+        )
+        plan = ctypes.c_void_p()
+        _lib.check(self._native.ws_plan_load(os.fsencode(path), descs, len(gpu_target), ctypes.byref(options), ctypes.byref(plan)))
+        self._plan = plan
+        self._finish(started, batch_bytes, "loaded", None)
+        self.stats["loaded_from"] = os.fspath(path)
+        return self
+
+    def save(self, path: str | os.PathLike) -> None:
+        """Write the package (descriptors, tables, checksums, encoded stream) to ``path``."""
+        _lib.check(self._native.ws_plan_save(self._plan, os.fsencode(path)))
+
+    def _finish(self, started: float, batch_bytes: int, encoder: str, dict_slack_pct: int | None) -> None:
+        with torch.cuda.device(self.device):
+            _lib.check(self._native.ws_plan_upload(self._plan, self.compute_stream.cuda_stream))
         self.last_apply: dict[str, Any] | None = None
         native = self.native_stats()
         counts = {name: int(native.mode_counts[i]) for i, name in enumerate(_lib.MODE_NAMES) if native.mode_counts[i]}
@@ -148,9 +200,9 @@ class DeltaWeights:
             "memory_scope": "Staging slots, descriptors and decode tables; excludes the CUDA context and allocator caching",
             "prepare_seconds": time.perf_counter() - started,
             # Additions of this implementation.
-            "policy": policy,
+            "policy": self.policy,
             "dict_slack_pct": dict_slack_pct,
-            "encoder": "gpu" if encode_on_device else "host",
+            "encoder": encoder,
             "block_bytes": _BLOCK_BYTES,
             "touched_bytes": int(native.touched_bytes),
             "zero_block_bytes": int(native.zero_block_bytes),
@@ -163,6 +215,13 @@ class DeltaWeights:
         """Validate the A/B layout and retain GPU storage bindings (delta.py:137-162)."""
         if not cpu_base or cpu_base.keys() != gpu_target.keys():
             raise ValueError("Delta tensor coverage differs")
+        self._bind_targets(gpu_target, cpu_base)
+
+    def _bind_targets(self, gpu_target: dict[str, torch.Tensor], cpu_base: dict[str, torch.Tensor] | None = None) -> None:
+        """The checks of delta.py:141-162 in their order; without ``cpu_base`` (a loaded
+        package) only the GPU side is checked."""
+        if not gpu_target:
+            raise ValueError("Delta tensor coverage differs")
         devices = {tensor.device for tensor in gpu_target.values()}
         if len(devices) != 1 or next(iter(devices)).type != "cuda":
             raise ValueError("Delta tensors must reside on one CUDA device")
@@ -172,10 +231,10 @@ class DeltaWeights:
         self.bindings = []
         spans = []
         for name, target in gpu_target.items():
-            base = cpu_base[name]
-            if base.device.type != "cpu" or base.shape != target.shape or base.dtype != target.dtype:
+            base = cpu_base[name] if cpu_base is not None else None
+            if base is not None and (base.device.type != "cpu" or base.shape != target.shape or base.dtype != target.dtype):
                 raise ValueError(f"Delta layout differs: {name}")
-            if not base.is_contiguous() or not target.is_contiguous():
+            if (base is not None and not base.is_contiguous()) or not target.is_contiguous():
                 raise ValueError(f"Delta requires contiguous tensors: {name}")
             size = target.numel() * target.element_size()
             if size:
