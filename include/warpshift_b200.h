@@ -142,9 +142,11 @@ WS_API int ws_plan_upload(ws_plan* plan, void* stream);
 WS_API int ws_plan_set_resident(ws_plan* plan, int resident, void* stream);
 
 /* Replaces DeltaWeights.apply (delta.py:294-327): A->B when reverse == 0, B->A when 1.
- * Stages the arena H2D on copy_stream in bounded batches, decodes and applies each
- * batch on compute_stream, reads back the device result, and returns after
- * compute_stream completes. Returns WS_ERR_DEVICE or WS_ERR_CHECKSUM on failure. */
+ * Stages the arena H2D on copy_stream in bounded batches (the first ones smaller),
+ * decodes and applies the batches alternately on compute_stream and a second
+ * stream of the plan that compute_stream joins at the end, reads back the device
+ * result, and returns after compute_stream completes. Returns WS_ERR_DEVICE or
+ * WS_ERR_CHECKSUM on failure. */
 WS_API int ws_apply(ws_plan* plan, int reverse, void* compute_stream, void* copy_stream, ws_apply_result* out);
 
 /* Asynchronous halves of ws_apply: enqueue only (no host synchronisation), then

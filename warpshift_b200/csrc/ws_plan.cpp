@@ -97,7 +97,9 @@ void release_device(ws_plan* p) {
   for (auto e : p->copy_done) cudaEventDestroy(e);
   for (auto e : p->compute_done) cudaEventDestroy(e);
   if (p->start_event) cudaEventDestroy(p->start_event);
+  if (p->aux_done) cudaEventDestroy(p->aux_done);
   if (p->own_copy_stream) cudaStreamDestroy(p->own_copy_stream);
+  if (p->aux_stream) cudaStreamDestroy(p->aux_stream);
   p->d_blocks = nullptr;
   p->d_tiles = nullptr;
   p->d_tables = nullptr;
@@ -108,7 +110,9 @@ void release_device(ws_plan* p) {
   p->copy_done.clear();
   p->compute_done.clear();
   p->start_event = nullptr;
+  p->aux_done = nullptr;
   p->own_copy_stream = nullptr;
+  p->aux_stream = nullptr;
   p->uploaded = false;
   if (prev >= 0) cudaSetDevice(prev);
 }
@@ -345,7 +349,9 @@ int form_batches(ws_plan* p, std::string* err) {
   p->batches.clear();
   // Batches: contiguous tile ranges of one arena chunk whose payload fits one
   // staging slot. A tile never spans chunks (chunks end at packet boundaries).
-  const uint64_t limit = p->opts.batch_bytes;
+  // The first batches are smaller (batch_bytes / 16, then / 4) so the first
+  // kernel starts after a short copy instead of a whole staging slot.
+  uint64_t limit = std::max<uint64_t>(p->opts.batch_bytes / 16, 1ull << 20);
   Batch cur{0, 0, 0, 0, 0};
   bool open = false;
   uint32_t chunk = 0;
@@ -362,6 +368,7 @@ int form_batches(ws_plan* p, std::string* err) {
     if (open && (cur.bytes + bytes > limit || cur.chunk != chunk)) {
       p->batches.push_back(cur);
       open = false;
+      limit = std::min(limit * 4, p->opts.batch_bytes);
     }
     if (!open) {
       cur = Batch{t, t, first.src, 0, chunk};
@@ -511,6 +518,8 @@ int ws_plan_upload(ws_plan* p, void* stream) {
   if (e == cudaSuccess) e = ws::prime_kernels();
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->start_event, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p->own_copy_stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->aux_done, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p->aux_stream, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) {
     std::string msg = std::string("upload: ") + cudaGetErrorString(e);
@@ -571,24 +580,32 @@ int ws_apply_async(ws_plan* p, int reverse, void* compute_stream, void* copy_str
       launches = 1;
     }
   } else {
+    // Staged: batch b is copied into slot b % nslots on the copy stream and
+    // decoded on compute stream b % 2 (the caller's stream or the plan's second
+    // one), so one batch's kernel fills the SMs the previous kernel's last wave
+    // leaves idle. Slot reuse waits for the kernel that read the slot.
     const size_t nslots = p->d_slots.size();
     WS_CUDA_TRY(cudaEventRecord(p->start_event, comp));
     WS_CUDA_TRY(cudaStreamWaitEvent(copy, p->start_event, 0));
+    WS_CUDA_TRY(cudaStreamWaitEvent(p->aux_stream, p->start_event, 0));
     for (size_t b = 0; b < p->batches.size(); ++b) {
       const Batch& bt = p->batches[b];
       const size_t slot = b % nslots;
+      cudaStream_t run = (b & 1) ? p->aux_stream : comp;
       if (b >= nslots) WS_CUDA_TRY(cudaStreamWaitEvent(copy, p->compute_done[slot], 0));
       const ws::ArenaChunk& ch = p->chunks[bt.chunk];
       WS_CUDA_TRY(cudaMemcpyAsync(p->d_slots[slot], ch.ptr + (bt.arena_off - ch.off), bt.bytes,
                                   cudaMemcpyHostToDevice, copy));
       WS_CUDA_TRY(cudaEventRecord(p->copy_done[slot], copy));
-      WS_CUDA_TRY(cudaStreamWaitEvent(comp, p->copy_done[slot], 0));
+      WS_CUDA_TRY(cudaStreamWaitEvent(run, p->copy_done[slot], 0));
       WS_CUDA_TRY(ws::launch_apply(p->d_tiles, bt.tile_begin, bt.tile_end - bt.tile_begin, p->d_blocks, p->d_tables,
-                                   p->d_slots[slot], bt.arena_off, p->d_result, reverse, comp));
-      WS_CUDA_TRY(cudaEventRecord(p->compute_done[slot], comp));
+                                   p->d_slots[slot], bt.arena_off, p->d_result, reverse, run));
+      WS_CUDA_TRY(cudaEventRecord(p->compute_done[slot], run));
       h2d += bt.bytes;
       ++launches;
     }
+    WS_CUDA_TRY(cudaEventRecord(p->aux_done, p->aux_stream));
+    WS_CUDA_TRY(cudaStreamWaitEvent(comp, p->aux_done, 0));
   }
   WS_CUDA_TRY(cudaMemcpyAsync(p->h_result, p->d_result, sizeof(ws_device_result), cudaMemcpyDeviceToHost, comp));
   p->pending_reverse = reverse;

@@ -48,7 +48,9 @@ struct ws_plan {
   ws_device_result* h_result = nullptr;
   std::vector<cudaEvent_t> copy_done, compute_done;
   cudaEvent_t start_event = nullptr;
+  cudaEvent_t aux_done = nullptr;        // end of the second compute stream's work
   cudaStream_t own_copy_stream = nullptr;
+  cudaStream_t aux_stream = nullptr;     // runs every other staging batch's kernel
 
   int pending_reverse = -1;
   uint64_t pending_h2d = 0;
