@@ -258,9 +258,10 @@ class OracleSwitch:
         self.tensors = len(a)
         self.reverse = True  # b holds Teacher2
 
-    def switch(self) -> float:
+    def switch(self, threads: int | None = None) -> float:
         t0 = time.perf_counter()
-        err, ck = self.ostream.apply_plan(self.blocks, self.tiles, self.tables, self.arena, 0, self.reverse, self.cores)
+        err, ck = self.ostream.apply_plan(self.blocks, self.tiles, self.tables, self.arena, 0, self.reverse,
+                                          threads or self.cores)
         dt = time.perf_counter() - t0
         if err or ck != self.expected[1 if self.reverse else 0]:
             raise RuntimeError("CPU baseline produced wrong bytes")
@@ -276,14 +277,21 @@ class OracleSwitch:
 
 
 def cpu_baseline(a, b, policy: str, seconds: float) -> dict:
+    """All host cores for ~`seconds`, then one core for a short bounded sample."""
     sw = OracleSwitch(a, b, policy)
     steps, elapsed = 0, 0.0
     while elapsed < seconds or steps < 2:
         elapsed += sw.switch()
         steps += 1
+    one_steps, one_elapsed = 0, 0.0
+    while one_elapsed < min(5.0, seconds / 2) or one_steps < 1:
+        one_elapsed += sw.switch(threads=1)
+        one_steps += 1
     sw.close()
     return {"value": round(steps * sw.bytes / elapsed / 1e9, 3), "unit": UNIT, "cores": sw.cores, "kind": "port",
-            "sample": sw.describe(steps), "seconds": round(elapsed, 2)}
+            "sample": sw.describe(steps), "seconds": round(elapsed, 2),
+            "single_core": {"value": round(one_steps * sw.bytes / one_elapsed / 1e9, 3), "unit": UNIT, "cores": 1,
+                            "switches": one_steps}}
 
 
 # --------------------------------------------------------------------------- arms

@@ -84,7 +84,13 @@ typedef struct ws_plan_stats {
   uint64_t blocks, tiles, batches, packets;
   uint64_t expected_checksum[2]; /* [0] after forward (A->B), [1] after reverse (B->A) */
   double encode_seconds;
+  uint32_t encoder;            /* WS_ENCODER_*: which path produced the plan */
+  uint32_t reserved;
 } ws_plan_stats;
+
+#define WS_ENCODER_HOST 0   /* host threads (B copied device->host, or host targets) */
+#define WS_ENCODER_GPU 1    /* GPU encoder */
+#define WS_ENCODER_LOADED 2 /* ws_plan_load of a saved plan */
 
 typedef struct ws_apply_result {
   uint64_t checksum;         /* checksum of the bytes written by this apply */
@@ -127,9 +133,11 @@ WS_API int ws_u16_residual(const uint8_t* base, const uint8_t* target, uint64_t 
  * encode_on_device, A is copied host->device in encode_batch_bytes batches (pageable A staged
  * through pinned buffers by up to `threads` host threads) and every packet is
  * encoded on the device on `stream`; the payloads come back into the host arena and
- * the temporary device buffers are freed before returning. Otherwise B is copied
- * device->host in 16 MiB packets and encoded on `threads` host threads. Both
- * encoders produce byte-identical plans. */
+ * the temporary device buffers are freed before returning. If the device cannot
+ * hold the encoder's buffers, the GPU encoder retries with batches 4x smaller (down
+ * to 32 MiB) and then falls back to the host encoder; ws_plan_stats.encoder says
+ * which ran. Otherwise B is copied device->host in 16 MiB packets and encoded on
+ * `threads` host threads. Both encoders produce byte-identical plans. */
 WS_API int ws_plan_build(const ws_tensor_desc* tensors, uint64_t ntensors, const ws_build_options* opts,
                   void* stream, ws_plan** out);
 

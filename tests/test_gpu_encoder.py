@@ -122,3 +122,45 @@ def test_gpu_encoder_arena_in_several_chunks(cuda_device) -> None:
     finally:
         lib.ws_plan_destroy(p_gpu)
         lib.ws_plan_destroy(p_host)
+
+
+def fill_device(cuda_device, leave: int) -> list:
+    """Hold all but about `leave` bytes of free device memory in torch tensors."""
+    torch.cuda.empty_cache()
+    held = []
+    free, _ = torch.cuda.mem_get_info(cuda_device)
+    chunk = 1 << 30
+    while free > leave + (2 << 20):
+        size = min(chunk, free - leave)
+        try:
+            held.append(torch.empty(size, dtype=torch.uint8, device=cuda_device))
+        except torch.OutOfMemoryError:
+            if chunk <= (2 << 20):
+                break
+            chunk //= 2
+        free, _ = torch.cuda.mem_get_info(cuda_device)
+    return held
+
+
+@pytest.mark.parametrize("leave_mb, encoder", [(190, "gpu"), (60, "host")])
+def test_gpu_encoder_under_memory_pressure(cuda_device, leave_mb: int, encoder: str) -> None:
+    """With little free HBM the GPU encoder retries with smaller batches (512 ->
+    128 -> 32 MiB), then hands over to the host encoder; the plan is the same."""
+    x, y = bf16_pair((96 << 20) // 2, 0.01, 31)
+    b_dev = {"w": y.to(cuda_device)}
+    lib = _lib.load()
+    p_host = build({"w": x}, b_dev, "auto", 6, False)
+    held = fill_device(cuda_device, leave_mb << 20)
+    try:
+        p_gpu = build({"w": x}, b_dev, "auto", 6, True)
+    finally:
+        del held
+        torch.cuda.empty_cache()
+    try:
+        stats = _lib.PlanStats()
+        _lib.check(lib.ws_plan_get_stats(p_gpu, ctypes.byref(stats)))
+        assert _lib.ENCODERS[stats.encoder] == encoder
+        assert_same_plan(p_gpu, p_host)
+    finally:
+        lib.ws_plan_destroy(p_gpu)
+        lib.ws_plan_destroy(p_host)

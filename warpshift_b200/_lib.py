@@ -57,6 +57,8 @@ class PlanStats(ctypes.Structure):
         ("packets", u64),
         ("expected_checksum", u64 * 2),
         ("encode_seconds", ctypes.c_double),
+        ("encoder", u32),
+        ("reserved", u32),
     ]
 
 
@@ -105,6 +107,7 @@ SIGNATURES = {
     "ws_tensor_hashes": ([ctypes.POINTER(P), ctypes.POINTER(u64), u64, ctypes.c_int, P, ctypes.POINTER(u64)], ctypes.c_int),
 }
 WS_NOALLOC_MAX_TILES = 16384
+ENCODERS = {0: "host", 1: "gpu", 2: "loaded"}
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

@@ -608,6 +608,7 @@ void free_host_chunk(const ArenaChunk& c) {
   do {                                                                               \
     cudaError_t e_ = (expr);                                                         \
     if (e_ != cudaSuccess) {                                                         \
+      if (e_ == cudaErrorMemoryAllocation) *device_oom = true;                       \
       *err = std::string("GPU encoder: ") + #expr + ": " + cudaGetErrorString(e_);   \
       return false;                                                                  \
     }                                                                                \
@@ -615,7 +616,9 @@ void free_host_chunk(const ArenaChunk& c) {
 
 bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, int dict_slack_pct,
                         uint64_t batch_bytes, int threads, bool pin, cudaStream_t stream,
-                        std::vector<EncodedPacket>* out, std::vector<ArenaChunk>* chunks, std::string* err) {
+                        std::vector<EncodedPacket>* out, std::vector<ArenaChunk>* chunks, std::string* err,
+                        bool* device_oom) {
+  *device_oom = false;
   out->resize(packets.size());
   int device = 0;
   WS_GPU_TRY(cudaGetDevice(&device));

@@ -39,9 +39,12 @@ void free_host_chunk(const ArenaChunk& chunk);
 // they are copied, in arena order, into host chunks appended to *chunks
 // (pinned when `pin` is set; the caller frees them, also after a failure).
 // Pageable A bytes are staged through pinned buffers by up to `threads` host
-// threads. Returns false with *err set on a CUDA or allocation error.
+// threads. Returns false with *err set on a CUDA or allocation error;
+// *device_oom tells whether a device allocation was what failed (the caller may
+// retry with smaller batches).
 bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, int dict_slack_pct,
                         uint64_t batch_bytes, int threads, bool pin, cudaStream_t stream,
-                        std::vector<EncodedPacket>* out, std::vector<ArenaChunk>* chunks, std::string* err);
+                        std::vector<EncodedPacket>* out, std::vector<ArenaChunk>* chunks, std::string* err,
+                        bool* device_oom);
 
 }  // namespace ws

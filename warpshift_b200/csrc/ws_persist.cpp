@@ -320,6 +320,7 @@ int ws_plan_load(const char* path, const ws_tensor_desc* tensors, uint64_t ntens
     if (rc != WS_OK) return reject(rc, err);
   }
   p->stats.scratch_bytes = 0;
+  p->stats.encoder = WS_ENCODER_LOADED;
   p->stats.encode_seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - started).count();
   *out = p;
   return WS_OK;

@@ -145,13 +145,22 @@ int encode_all(const ws_tensor_desc* tensors, const std::vector<PacketRef>& pack
       in.push_back(ws::GpuPacketInput{(const uint8_t*)t.base + pr.offset, (const uint8_t*)t.target + pr.offset,
                                       pr.nbytes, t.is_bf16 != 0});
     }
-    std::string err;
-    *external = true;
-    const uint64_t batch = o.encode_batch_bytes ? o.encode_batch_bytes : (512ull << 20);
-    if (!ws::gpu_encode_packets(in, o.policy, o.dict_slack_pct, batch, threads, o.pin_arena != 0, stream, out,
-                                chunks, &err))
-      return fail(WS_ERR_CUDA, err);
-    return WS_OK;
+    // A serving process may have given most free HBM to its KV cache: on a device
+    // allocation failure retry with smaller batches, then use the host encoder.
+    for (uint64_t batch = o.encode_batch_bytes ? o.encode_batch_bytes : (512ull << 20);; batch /= 4) {
+      std::string err;
+      bool oom = false;
+      if (ws::gpu_encode_packets(in, o.policy, o.dict_slack_pct, batch, threads, o.pin_arena != 0, stream, out,
+                                 chunks, &err, &oom)) {
+        *external = true;
+        return WS_OK;
+      }
+      free_chunks(chunks);
+      out->assign(packets.size(), ws::EncodedPacket());
+      if (!oom) return fail(WS_ERR_CUDA, err);
+      cudaGetLastError();  // allocation failures are not sticky; clear the record
+      if (batch / 4 < (32ull << 20)) break;
+    }
   }
   if (!o.target_on_device) {
     parallel_for(packets.size(), threads, [&](uint64_t i) {
@@ -466,6 +475,7 @@ int ws_plan_build(const ws_tensor_desc* tensors, uint64_t ntensors, const ws_bui
   int rc = encode_all(tensors, packets, p->opts, (cudaStream_t)stream, &enc, &p->chunks, &external);
   const auto t_lay = std::chrono::steady_clock::now();
   if (rc == WS_OK) rc = layout(p, tensors, packets, enc, external);
+  p->stats.encoder = external ? WS_ENCODER_GPU : WS_ENCODER_HOST;
   if (getenv("WS_ENCODER_TIMING"))
     fprintf(stderr, "plan build: encode %.3f s, layout %.3f s\n",
             std::chrono::duration<double>(t_lay - t_enc).count(),

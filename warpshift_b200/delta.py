@@ -92,6 +92,7 @@ class DeltaWeights:
         staging_slots: int = 3,
         dict_slack_pct: int = _DICT_SLACK_PCT,
         encode_on_device: bool = True,
+        encode_batch_bytes: int = 0,
     ) -> None:
         started = time.perf_counter()
         if policy not in _lib.POLICIES:
@@ -122,13 +123,14 @@ class DeltaWeights:
             pin_arena=1,
             dict_slack_pct=dict_slack_pct,
             encode_on_device=int(bool(encode_on_device)),
+            encode_batch_bytes=encode_batch_bytes,
         )
         plan = ctypes.c_void_p()
         with torch.cuda.device(self.device):
             stream = self.compute_stream.cuda_stream
             _lib.check(self._native.ws_plan_build(descs, len(gpu_target), ctypes.byref(options), stream, ctypes.byref(plan)))
             self._plan = plan
-        self._finish(started, batch_bytes, "gpu" if encode_on_device else "host", dict_slack_pct)
+        self._finish(started, batch_bytes, dict_slack_pct)
 
     @classmethod
     def load(
@@ -169,7 +171,7 @@ class DeltaWeights:
         plan = ctypes.c_void_p()
         _lib.check(self._native.ws_plan_load(os.fsencode(path), descs, len(gpu_target), ctypes.byref(options), ctypes.byref(plan)))
         self._plan = plan
-        self._finish(started, batch_bytes, "loaded", None)
+        self._finish(started, batch_bytes, None)
         self.stats["loaded_from"] = os.fspath(path)
         return self
 
@@ -177,7 +179,7 @@ class DeltaWeights:
         """Write the package (descriptors, tables, checksums, encoded stream) to ``path``."""
         _lib.check(self._native.ws_plan_save(self._plan, os.fsencode(path)))
 
-    def _finish(self, started: float, batch_bytes: int, encoder: str, dict_slack_pct: int | None) -> None:
+    def _finish(self, started: float, batch_bytes: int, dict_slack_pct: int | None) -> None:
         with torch.cuda.device(self.device):
             _lib.check(self._native.ws_plan_upload(self._plan, self.compute_stream.cuda_stream))
         self.last_apply: dict[str, Any] | None = None
@@ -202,7 +204,7 @@ class DeltaWeights:
             # Additions of this implementation.
             "policy": self.policy,
             "dict_slack_pct": dict_slack_pct,
-            "encoder": encoder,
+            "encoder": _lib.ENCODERS.get(int(native.encoder), "unknown"),
             "block_bytes": _BLOCK_BYTES,
             "touched_bytes": int(native.touched_bytes),
             "zero_block_bytes": int(native.zero_block_bytes),
