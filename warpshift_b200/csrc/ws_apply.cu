@@ -414,13 +414,19 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
   {
     uint32_t next_event = 0;
     uint4* p = reinterpret_cast<uint4*>(dst + lane * 16u);
-    // The destination vector of group g + 1 is loaded while group g decodes,
-    // and groups further ahead are pulled into L2 by the TMA unit, so the DRAM
-    // latency of the destination stream stays hidden at high bandwidth.
+    // Dictionary blocks (HBM-bound): the destination vector of group g + 1 is
+    // loaded while group g decodes, and groups further ahead are pulled into L2
+    // by the TMA unit, so the DRAM latency of the destination stream stays
+    // hidden at high bandwidth. Byte-plane blocks are bound by instruction
+    // issue (two symbols per word): the four checks of a group hide the plain
+    // load's latency, and the look-ahead would cost ~29 instructions a group.
     uint4 next_old = make_uint4(0, 0, 0, 0);
-    if (lane == 0)
-      for (uint32_t k = 1; k <= kPrefetchGroups && k < fast_groups; ++k) prefetch_l2(dst + k * WS_GROUP_BYTES, WS_GROUP_BYTES);
-    if (fast_groups > 0) next_old = ldg128_early(p);
+    if (DICT) {
+      if (lane == 0)
+        for (uint32_t k = 1; k <= kPrefetchGroups && k < fast_groups; ++k)
+          prefetch_l2(dst + k * WS_GROUP_BYTES, WS_GROUP_BYTES);
+      if (fast_groups > 0) next_old = ldg128_early(p);
+    }
 #pragma unroll 1
     for (; g < fast_groups; ++g, p += WS_GROUP_BYTES / 16) {
       if (pos >= next_event) {
@@ -431,10 +437,15 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
             (ready < issued && bd.nwords > kHalfHalfwords * ready) ? kHalfHalfwords * ready - 255u : 0xFFFFFFFFu;
         next_event = min(recycle, wait);
       }
-      const uint4 old = next_old;
-      if (g + 1 < fast_groups) next_old = ldg128_early(p + WS_GROUP_BYTES / 16);
-      if (lane == 0 && g + 1 + kPrefetchGroups < fast_groups)
-        prefetch_l2(dst + (g + 1 + kPrefetchGroups) * WS_GROUP_BYTES, WS_GROUP_BYTES);
+      uint4 old;
+      if (DICT) {
+        old = next_old;
+        if (g + 1 < fast_groups) next_old = ldg128_early(p + WS_GROUP_BYTES / 16);
+        if (lane == 0 && g + 1 + kPrefetchGroups < fast_groups)
+          prefetch_l2(dst + (g + 1 + kPrefetchGroups) * WS_GROUP_BYTES, WS_GROUP_BYTES);
+      } else {
+        old = *p;
+      }
       uint32_t rp = ring_s + (pos & (kRingHalfwords - 1)) * 2u;
       const uint32_t rp0 = rp;
       uint32_t r0, r1, r2, r3;
