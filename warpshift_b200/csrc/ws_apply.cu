@@ -128,18 +128,21 @@ __device__ __forceinline__ void report(ws_device_result* res, uint32_t err, uint
   atomicExch(&res->bad_block_plus1, block + 1);
 }
 
-// d = unzigzag in rotated form: y ^ (sign ? 0x7FFF : 0) per 16-bit half.
-// Returns d & 0x7FFF7FFF in *dm; bit 15 of each half of d equals that of y.
+// U16 apply on two 16-bit words at once. The coded word y is the rotated
+// zigzag of d = B - A, so d = y ^ (bit 15 of y ? 0x7FFF : 0) per half; the new
+// word is old + d (forward) or old - d (reverse), wrapping per half. The 16x2
+// SIMD add does the per-half wrap in one instruction; reverse adds the
+// per-half two's complement ~d + 1.
+__device__ __forceinline__ uint32_t add16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 __device__ __forceinline__ uint32_t u16_apply(uint32_t old, uint32_t y, bool reverse) {
-  const uint32_t sign = prmt(y, 0, 0xBB99);          // 0xFFFF per half with bit 15 set
-  const uint32_t dm = (y ^ sign) & 0x7FFF7FFFu;      // low 15 bits of d
-  if (!reverse) {
-    const uint32_t s = (old & 0x7FFF7FFFu) + dm;
-    return s ^ ((old ^ y) & 0x80008000u);
-  } else {
-    const uint32_t s = (old | 0x80008000u) - dm;
-    return s ^ ((old ^ y ^ 0x80008000u) & 0x80008000u);
-  }
+  const uint32_t d = y ^ (prmt(y, 0, 0xBB99) & 0x7FFF7FFFu);  // prmt: 0xFFFF per half with bit 15 set
+  if (!reverse) return add16x2(old, d);
+  return add16x2(old, add16x2(~d, 0x00010001u));
 }
 
 struct Checksum {
