@@ -300,6 +300,16 @@ def cpu_baseline(a, b, policy: str, seconds: float) -> dict:
                             "switches": one_steps}}
 
 
+def per_direction(ms: list, reverse: list) -> dict:
+    """Median step time per switch direction (the reference's validate.py:272-293 reports medians)."""
+    out = {}
+    for label, flag in (("A->B", False), ("B->A", True)):
+        xs = [m for m, r in zip(ms, reverse) if r == flag]
+        if xs:
+            out[label] = round(statistics.median(xs), 3)
+    return out
+
+
 # --------------------------------------------------------------------------- arms
 def run_reference(args) -> None:
     """Reference arm: the oracle's CPU switch on all host cores, rank 0 only."""
@@ -412,6 +422,9 @@ def run_ours(args) -> None:
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     launches_k = 0
+    k_reverse: list[bool] = []  # direction of each timed step (True: B -> A)
+    e_reverse: list[bool] = []
+    e_step_ms: list[float] = []
     with sampler:
         barrier()
         t_begin = torch.cuda.Event(enable_timing=True)
@@ -421,6 +434,7 @@ def run_ours(args) -> None:
             starts[k].record(stream)
             delta.apply_async(reverse=state_is_b)
             ends[k].record(stream)
+            k_reverse.append(state_is_b)
             state_is_b = not state_is_b
             launches_k += 1
         t_end.record(stream)
@@ -442,17 +456,22 @@ def run_ours(args) -> None:
             barrier()
             caller = torch.cuda.current_stream(device)
             e_begin, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e_marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
             e_begin.record(caller)
+            e_marks[0].record(caller)
             for k in range(args.steps):
                 delta.apply(reverse=state_is_b)
                 if group is not None:
                     delta.confirm(group)
+                e_marks[k + 1].record(caller)
                 launches_e += delta.last_apply["launches"]
+                e_reverse.append(state_is_b)
                 state_is_b = not state_is_b
             e_end.record(caller)
             torch.cuda.synchronize(device)
             barrier()
             e2e_ms = e_begin.elapsed_time(e_end)
+            e_step_ms = [a.elapsed_time(b) for a, b in zip(e_marks, e_marks[1:])]
     clocks = sampler.summary()
 
     full_copy = None
@@ -560,6 +579,7 @@ def run_ours(args) -> None:
             "encode_seconds": round(stats["encode_seconds"], 2),
             "parallelism": f"{world} independent rank shard(s), NCCL checksum all-reduce per switch" if world > 1 else "1 GPU",
             "kernel_step_ms": [round(x, 3) for x in step_ms],
+            "kernel_median_ms": per_direction(step_ms, k_reverse),
         },
         "e2e": None if e2e_value is None else {
             "value": round(e2e_value, 2),
@@ -572,6 +592,7 @@ def run_ours(args) -> None:
             "roofline_ms": round(t_roof_ms, 3),
             "roofline_frac": round(t_roof_ms / (e2e_ms_max / args.steps), 3),
             "launches": launches_e,
+            "median_ms": per_direction(e_step_ms, e_reverse),
         },
         "roofline": {
             "bound": "hbm",
