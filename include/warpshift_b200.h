@@ -212,6 +212,15 @@ WS_API int ws_plan_load(const char* path, const ws_tensor_desc* tensors, uint64_
 WS_API int ws_tensor_hashes(const void* const* ptrs, const uint64_t* nbytes, uint64_t n, int device, void* stream,
                             uint64_t* out);
 
+/* No counterpart in the reference. Failure-path self-test: one warp waits on a
+ * staging barrier that nothing arrives on, with the decode kernel's bounded wait
+ * limited to `polls` (1 .. 2^20) polls; the wait gives up and the warp reports
+ * through the device result word. *device_errors receives the reported bits
+ * (WS_DEVERR_TIMEOUT = 4 expected). Nothing faults or hangs; the context stays
+ * usable. Allocates one 16-byte stream-ordered buffer; returns after `stream`
+ * completes. */
+WS_API int ws_selftest_wait_timeout(uint32_t polls, int device, void* stream, uint32_t* device_errors);
+
 /* Frees host and device resources (delta.py relies on GC for the same). */
 WS_API void ws_plan_destroy(ws_plan* plan);
 

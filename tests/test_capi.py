@@ -35,3 +35,13 @@ def test_version_and_error_buffer_without_a_gpu() -> None:
     assert lib.ws_version() >= 100
     assert lib.ws_u16_residual(None, None, 3, None) == _lib.WS_ERR_INVALID
     assert "even" in _lib.last_error()
+
+
+def test_self_test_rejects_bad_arguments_without_a_gpu() -> None:
+    import ctypes
+
+    lib = _lib.load()
+    errors = ctypes.c_uint32(0)
+    assert lib.ws_selftest_wait_timeout(0, 0, None, ctypes.byref(errors)) == _lib.WS_ERR_INVALID
+    assert lib.ws_selftest_wait_timeout((1 << 20) + 1, 0, None, ctypes.byref(errors)) == _lib.WS_ERR_INVALID
+    assert lib.ws_selftest_wait_timeout(10, 0, None, None) == _lib.WS_ERR_INVALID

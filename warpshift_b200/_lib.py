@@ -104,6 +104,7 @@ SIGNATURES = {
     "ws_apply_device_noalloc": ([P, u32, P, P, P, ctypes.c_int, ctypes.c_int, P, ctypes.POINTER(ApplyResult)], ctypes.c_int),
     "ws_plan_save": ([P, ctypes.c_char_p], ctypes.c_int),
     "ws_plan_load": ([ctypes.c_char_p, ctypes.POINTER(TensorDesc), u64, ctypes.POINTER(BuildOptions), ctypes.POINTER(P)], ctypes.c_int),
+    "ws_selftest_wait_timeout": ([u32, ctypes.c_int, P, ctypes.POINTER(u32)], ctypes.c_int),
     "ws_tensor_hashes": ([ctypes.POINTER(P), ctypes.POINTER(u64), u64, ctypes.c_int, P, ctypes.POINTER(u64)], ctypes.c_int),
 }
 WS_NOALLOC_MAX_TILES = 16384

@@ -110,8 +110,8 @@ __device__ __forceinline__ void bulk_load2(uint32_t dst0, uint32_t dst1, const v
 
 // Returns true when the phase with the given parity has completed, false if
 // the bounded wait gave up.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  for (uint32_t it = 0; it < kWaitLimit; ++it) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t limit = kWaitLimit) {
+  for (uint32_t it = 0; it < limit; ++it) {
     uint32_t ok;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
@@ -812,4 +812,58 @@ extern "C" WS_API int ws_apply_device_noalloc(const void* tiles, uint32_t ntiles
     return done(WS_ERR_DEVICE);
   }
   return done(WS_OK);
+}
+
+// ---------------------------------------------------------------------------
+// Failure-path self-test (ws_selftest_wait_timeout in include/warpshift_b200.h).
+// One warp waits, with the decode kernel's bounded wait, on a staging barrier
+// that nothing ever arrives on: the wait gives up after `limit` polls and the
+// warp reports WS_DEVERR_TIMEOUT through the usual result word, leaving no copy
+// in flight, so the context stays usable. No fault, trap or endless loop.
+namespace ws {
+namespace {
+
+__global__ void ws_wait_selftest_kernel(uint32_t limit, ws_device_result* res) {
+  __shared__ __align__(8) uint64_t bar;
+  const uint32_t b = smem_addr(&bar);
+  if (threadIdx.x == 0) {
+    mbar_init(b, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  if (!mbar_wait(b, 0, limit) && threadIdx.x == 0) report(res, WS_DEVERR_TIMEOUT, 0);
+}
+
+}  // namespace
+}  // namespace ws
+
+extern "C" WS_API int ws_selftest_wait_timeout(uint32_t polls, int device, void* stream, uint32_t* device_errors) {
+  using namespace ws;
+  if (!device_errors || polls == 0 || polls > kWaitLimit) {
+    set_last_error("ws_selftest_wait_timeout: need 1 <= polls <= 2^20 and a result pointer");
+    return WS_ERR_INVALID;
+  }
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaError_t e = cudaSetDevice(device);
+  ws_device_result* d = nullptr;
+  ws_device_result h{};
+  cudaStream_t s = (cudaStream_t)stream;
+  if (e == cudaSuccess) e = cudaMallocAsync((void**)&d, sizeof(ws_device_result), s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(d, 0, sizeof(ws_device_result), s);
+  if (e == cudaSuccess) {
+    ws_wait_selftest_kernel<<<1, 32, 0, s>>>(polls, d);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&h, d, sizeof(h), cudaMemcpyDeviceToHost, s);
+  if (d) cudaFreeAsync(d, s);
+  const cudaError_t es = cudaStreamSynchronize(s);
+  if (e == cudaSuccess) e = es;
+  if (prev >= 0) cudaSetDevice(prev);
+  if (e != cudaSuccess) {
+    set_last_error((std::string("ws_selftest_wait_timeout: ") + cudaGetErrorString(e)).c_str());
+    return WS_ERR_CUDA;
+  }
+  *device_errors = h.errors;
+  return WS_OK;
 }
