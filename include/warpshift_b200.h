@@ -58,7 +58,7 @@ typedef struct ws_build_options {
   int32_t threads;          /* host encoder threads; 0 = all online CPUs */
   int32_t target_on_device; /* 1: target pointers are device addresses (normal prepare) */
   int32_t device;           /* CUDA device ordinal of the targets */
-  uint64_t batch_bytes;     /* bound on one H2D staging batch (0 = 16 MiB) */
+  uint64_t batch_bytes;     /* bound on one H2D staging batch (0 = 64 MiB, delta.py:21) */
   int32_t staging_slots;    /* device staging buffers (0 = 3) */
   int32_t pin_arena;        /* 1: arena in pinned host memory (needs CUDA); 0: malloc */
   int32_t dict_slack_pct;   /* code a packet as one symbol per word (word dictionary) when its words

@@ -255,7 +255,7 @@ int ws_plan_load(const char* path, const ws_tensor_desc* tensors, uint64_t ntens
     return fail(code, msg);
   };
   p->opts = *opts;
-  if (p->opts.batch_bytes == 0) p->opts.batch_bytes = 16ull << 20;
+  if (p->opts.batch_bytes == 0) p->opts.batch_bytes = 64ull << 20;
   if (p->opts.batch_bytes < (2ull << 20)) return reject(WS_ERR_INVALID, "batch_bytes must be at least 2 MiB");
   if (p->opts.staging_slots <= 0) p->opts.staging_slots = 3;
   p->device = opts->target_on_device ? opts->device : -1;

@@ -335,13 +335,13 @@ int layout(ws_plan* p, const ws_tensor_desc* tensors, const std::vector<PacketRe
     if (covered != arena) return fail(WS_ERR_STATE, "internal: arena chunks do not match the block layout");
   }
   if (p->blocks.size() > 0xFFFFFFFFull) return fail(WS_ERR_INVALID, "too many blocks in one plan");
+  p->arena_bytes = arena;
+  st.arena_bytes = arena;
   {
     std::string err;
     const int rc = ws::form_batches(p, &err);
     if (rc != WS_OK) return fail(rc, err);
   }
-  p->arena_bytes = arena;
-  st.arena_bytes = arena;
   st.table_bytes = p->tables.size() * 4;
   st.metadata_bytes = p->blocks.size() * sizeof(ws_block_desc) + p->tiles.size() * sizeof(ws_tile_desc) +
                       st.table_bytes;
@@ -358,9 +358,13 @@ int form_batches(ws_plan* p, std::string* err) {
   p->batches.clear();
   // Batches: contiguous tile ranges of one arena chunk whose payload fits one
   // staging slot. A tile never spans chunks (chunks end at packet boundaries).
-  // The first batches are smaller (batch_bytes / 16, then / 4) so the first
-  // kernel starts after a short copy instead of a whole staging slot.
-  uint64_t limit = std::max<uint64_t>(p->opts.batch_bytes / 16, 1ull << 20);
+  // Batches grow to `cap`: batch_bytes for large streams (fewer, longer copies),
+  // down to 16 MiB for small ones (about 64 batches per stream keep the kernels
+  // of consecutive batches overlapping). The first batches are smaller (cap / 16,
+  // then / 4) so the first kernel starts after a short copy.
+  const uint64_t cap =
+      std::min<uint64_t>(p->opts.batch_bytes, std::max<uint64_t>(16ull << 20, p->arena_bytes / 64));
+  uint64_t limit = std::max<uint64_t>(cap / 16, 1ull << 20);
   Batch cur{0, 0, 0, 0, 0};
   bool open = false;
   uint32_t chunk = 0;
@@ -377,7 +381,7 @@ int form_batches(ws_plan* p, std::string* err) {
     if (open && (cur.bytes + bytes > limit || cur.chunk != chunk)) {
       p->batches.push_back(cur);
       open = false;
-      limit = std::min(limit * 4, p->opts.batch_bytes);
+      limit = std::min(limit * 4, cap);
     }
     if (!open) {
       cur = Batch{t, t, first.src, 0, chunk};
@@ -428,7 +432,7 @@ int ws_plan_build(const ws_tensor_desc* tensors, uint64_t ntensors, const ws_bui
   ws_plan* p = new (std::nothrow) ws_plan();
   if (!p) return fail(WS_ERR_NOMEM, "out of memory");
   p->opts = *opts;
-  if (p->opts.batch_bytes == 0) p->opts.batch_bytes = 16ull << 20;
+  if (p->opts.batch_bytes == 0) p->opts.batch_bytes = 64ull << 20;
   if (p->opts.batch_bytes < (2ull << 20)) {
     delete p;
     return fail(WS_ERR_INVALID, "batch_bytes must be at least 2 MiB");
