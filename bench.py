@@ -48,6 +48,8 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", default="llama3-8b", choices=["llama3-8b", "llama3-70b", "mixtral-8x7b", "qwen2-0.5b"])
+    p.add_argument("--escapes", type=int, default=0,
+                   help="word dictionaries with escape lists: 0 when smaller (default), -1 never, 1 whenever eligible")
     p.add_argument("--policy", default="xor", choices=["auto", "xor", "u16"])
     p.add_argument("--scale", type=float, default=0.01, help="relative perturbation s of Teacher2")
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline time budget")
@@ -374,7 +376,7 @@ def run_ours(args) -> None:
             if rank == 0 and world == 1 and not args.no_cpu_baseline:
                 sample = host_sample(spec, cpu_base, gpu, 1 << 30)
             t0 = time.perf_counter()
-            delta = DeltaWeights(cpu_base, gpu, policy=args.policy, threads=args.threads)
+            delta = DeltaWeights(cpu_base, gpu, policy=args.policy, threads=args.threads, escapes=args.escapes)
             prepare_s = time.perf_counter() - t0
             del cpu_base
         if group is not None:
@@ -569,6 +571,7 @@ def run_ours(args) -> None:
         "config": {
             "workload": desc,
             "policy": args.policy,
+            "escapes": args.escapes,
             "scale": args.scale,
             "weight_bytes_per_rank": W,
             "compressed_bytes_per_rank": C,

@@ -68,6 +68,9 @@ typedef struct ws_build_options {
                                copying only A host->device; 0: copy B device->host, encode on host threads */
   uint64_t encode_batch_bytes; /* GPU encoder: weight bytes encoded per device batch (0 = 512 MiB); the
                                   device holds up to about 4x this in temporary buffers during prepare */
+  int32_t escapes;          /* word dictionaries with escapes (rare words listed after each block's
+                               stream): 0 when estimated smaller, < 0 never, > 0 whenever eligible */
+  int32_t reserved;
 } ws_build_options;
 
 typedef struct ws_plan_stats {

@@ -27,6 +27,12 @@
  * freq = e >> 24. Lane l's state 0 decodes its words 0, 2, 4, 6 and state 1
  * its words 1, 3, 5, 7 of each group; a check follows every second word of
  * each state (after lane words 3 and 7), with the same read order.
+ *
+ * Dictionary blocks with flag 2 (escapes) carry, at byte (2 * nwords + 15) & ~15
+ * of the payload, uint16 count[32] and then count[0] + ... + count[31] uint32
+ * entries grouped by lane: word index (bits 0-15) | residual word (16-31). The
+ * listed words' residuals are the listed values (their stream symbol decodes
+ * as 0); an entry outside the block or not owned by its lane is an error.
  */
 #include <pthread.h>
 #include <stdint.h>
@@ -161,6 +167,23 @@ int wso_apply_block(const o_block* b, const uint8_t* payload, const uint32_t* ta
     return O_ERR_KIND;
   const int xor_apply = b->kind == O_ANS_XOR || b->kind == O_DICT_XOR;
   const uint32_t W = n / 2;
+  if ((b->kind == O_DICT_XOR || b->kind == O_DICT_U16) && (b->flags & 2u)) {
+    const uint32_t side = (2u * b->nwords + 15u) & ~15u;
+    if ((uint64_t)side + 64 > b->clen) return err | O_ERR_LENGTH;
+    uint32_t at = side + 64;
+    for (uint32_t l = 0; l < 32; ++l) {
+      const uint32_t count = rd16(payload + side + 2 * l);
+      if ((uint64_t)at + 4ull * count > b->clen) return err | O_ERR_LENGTH;
+      for (uint32_t k = 0; k < count; ++k, at += 4) {
+        const uint32_t e = rd32(payload + at), i = e & 0xFFFFu;
+        if (i >= W || (i % 256) / 8 != l) {
+          err |= O_ERR_LENGTH;
+          continue;
+        }
+        scratch_words[i] = (uint16_t)(e >> 16);
+      }
+    }
+  }
   for (uint32_t i = 0; i < W; ++i) {
     uint16_t old = rd16(dst + 2 * i), nw;
     if (xor_apply) {

@@ -54,7 +54,8 @@ def edge_pair(seed: int = 0, scale: float = 0.01, big: bool = True) -> tuple[dic
     return a, b
 
 
-def host_plan(a: dict[str, torch.Tensor], b: dict[str, torch.Tensor], policy: str, threads: int = 4, dict_slack_pct: int = 6):
+def host_plan(a: dict[str, torch.Tensor], b: dict[str, torch.Tensor], policy: str, threads: int = 4, dict_slack_pct: int = 6,
+              escapes: int = 0):
     """Build a plan on host targets (no GPU); b's tensors are the destinations."""
     lib = _lib.load()
     descs = (_lib.TensorDesc * len(a))()
@@ -64,7 +65,8 @@ def host_plan(a: dict[str, torch.Tensor], b: dict[str, torch.Tensor], policy: st
             int(b[name].dtype == torch.bfloat16), 0,
         )
     opts = _lib.BuildOptions(policy=_lib.POLICIES[policy], threads=threads, target_on_device=0, device=0,
-                             batch_bytes=0, staging_slots=0, pin_arena=0, dict_slack_pct=dict_slack_pct)
+                             batch_bytes=0, staging_slots=0, pin_arena=0, dict_slack_pct=dict_slack_pct,
+                             escapes=escapes)
     plan = ctypes.c_void_p()
     _lib.check(lib.ws_plan_build(descs, len(a), ctypes.byref(opts), None, ctypes.byref(plan)))
     return plan

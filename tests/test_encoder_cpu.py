@@ -27,7 +27,9 @@ def clone(d):
     return {k: v.clone() for k, v in d.items()}
 
 
-CODINGS = {"planes": -1, "default": 6, "dictionary": 100}
+# (dict_slack_pct, escapes): byte planes only, the default choice, a dictionary
+# wherever possible, and dictionaries with escape lists wherever eligible.
+CODINGS = {"planes": (-1, -1), "default": (6, 0), "dictionary": (100, -1), "escapes": (100, 1)}
 
 
 @pytest.mark.parametrize("coding", list(CODINGS))
@@ -35,7 +37,7 @@ CODINGS = {"planes": -1, "default": 6, "dictionary": 100}
 def test_host_plan_round_trips_through_the_oracle_decoder(policy: str, coding: str) -> None:
     a, b = edge_pair(seed=7)
     work = clone(b)
-    plan = host_plan(a, work, policy, dict_slack_pct=CODINGS[coding])
+    plan = host_plan(a, work, policy, dict_slack_pct=CODINGS[coding][0], escapes=CODINGS[coding][1])
     try:
         blocks, tiles, tables, arena, stats = plan_arrays(plan)
         assert stats.runtime_bytes == sum(t.numel() * t.element_size() for t in b.values())
@@ -73,7 +75,7 @@ def test_mode_rule_follows_the_reference() -> None:
 def test_coded_words_are_the_reference_residual(policy: str, coding: str) -> None:
     a_t, b_t = bf16_pair(3 * 32768 + 1000, 0.01, 9)
     a, b = {"w": a_t}, {"w": b_t.clone()}
-    plan = host_plan(a, b, policy, dict_slack_pct=CODINGS[coding])
+    plan = host_plan(a, b, policy, dict_slack_pct=CODINGS[coding][0], escapes=CODINGS[coding][1])
     try:
         blocks, tiles, tables, arena, stats = plan_arrays(plan)
         base, target = as_bytes(a_t), as_bytes(b_t)

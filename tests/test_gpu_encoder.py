@@ -20,7 +20,7 @@ from warpshift_b200 import _lib
 pytestmark = pytest.mark.gpu
 
 
-def build(a, b_dev, policy, slack, on_device, encode_batch_bytes=0, pin_arena=0, batch_bytes=0):
+def build(a, b_dev, policy, slack, on_device, encode_batch_bytes=0, pin_arena=0, batch_bytes=0, escapes=0):
     lib = _lib.load()
     descs = (_lib.TensorDesc * len(a))()
     for i, name in enumerate(b_dev):
@@ -29,7 +29,8 @@ def build(a, b_dev, policy, slack, on_device, encode_batch_bytes=0, pin_arena=0,
                                    int(t.dtype == torch.bfloat16), 0)
     opts = _lib.BuildOptions(policy=_lib.POLICIES[policy], threads=4, target_on_device=1, device=0,
                              batch_bytes=batch_bytes, staging_slots=0, pin_arena=pin_arena, dict_slack_pct=slack,
-                             encode_on_device=int(on_device), encode_batch_bytes=encode_batch_bytes)
+                             encode_on_device=int(on_device), encode_batch_bytes=encode_batch_bytes,
+                             escapes=escapes)
     plan = ctypes.c_void_p()
     stream = torch.cuda.current_stream().cuda_stream
     _lib.check(lib.ws_plan_build(descs, len(a), ctypes.byref(opts), stream, ctypes.byref(plan)))
@@ -49,14 +50,14 @@ def assert_same_plan(p_gpu, p_host) -> None:
     np.testing.assert_array_equal(ag, ah)
 
 
-@pytest.mark.parametrize("slack", [-1, 6, 100])
+@pytest.mark.parametrize("slack, escapes", [(-1, -1), (6, 0), (100, -1), (100, 1)])
 @pytest.mark.parametrize("policy", ["auto", "xor", "u16"])
-def test_gpu_encoder_matches_host_encoder(cuda_device, policy: str, slack: int) -> None:
+def test_gpu_encoder_matches_host_encoder(cuda_device, policy: str, slack: int, escapes: int) -> None:
     a, b = edge_pair(seed=13)
     b_dev = {k: v.to(cuda_device) for k, v in b.items()}
     lib = _lib.load()
-    p_gpu = build(a, b_dev, policy, slack, True)
-    p_host = build(a, b_dev, policy, slack, False)
+    p_gpu = build(a, b_dev, policy, slack, True, escapes=escapes)
+    p_host = build(a, b_dev, policy, slack, False, escapes=escapes)
     try:
         assert_same_plan(p_gpu, p_host)
     finally:

@@ -29,7 +29,7 @@ def assert_bytes_equal(gpu: dict[str, torch.Tensor], ref: dict[str, torch.Tensor
         np.testing.assert_array_equal(as_bytes(t), as_bytes(ref[name]), err_msg=name)
 
 
-CODINGS = {"planes": -1, "dictionary": 100}
+CODINGS = {"planes": (-1, -1), "dictionary": (100, -1), "escapes": (100, 1)}  # (dict_slack_pct, escapes)
 
 
 @pytest.mark.parametrize("coding", list(CODINGS))
@@ -37,7 +37,7 @@ CODINGS = {"planes": -1, "dictionary": 100}
 def test_edge_cases_round_trip_bit_exact(cuda_device, policy: str, coding: str) -> None:
     a, b = edge_pair(seed=1)
     gpu = to_device(b, cuda_device)
-    delta = DeltaWeights(a, gpu, policy=policy, dict_slack_pct=CODINGS[coding])
+    delta = DeltaWeights(a, gpu, policy=policy, dict_slack_pct=CODINGS[coding][0], escapes=CODINGS[coding][1])
     assert set(delta.stats) >= {
         "codec", "reversible", "chunk_bytes", "batch_bytes", "runtime_bytes", "skipped_bytes", "payload_bytes",
         "transferred_bytes", "pinned_bytes", "mode_counts", "batches", "gpu_scratch_bytes", "gpu_metadata_bytes",
@@ -56,7 +56,7 @@ def test_decoded_residual_matches_oracle(cuda_device, policy: str, coding: str) 
     """Apply onto zeroed weights: the kernel then writes the residual itself."""
     a, b = edge_pair(seed=2, big=False)
     gpu = to_device(b, cuda_device)
-    delta = DeltaWeights(a, gpu, policy=policy, dict_slack_pct=CODINGS[coding])
+    delta = DeltaWeights(a, gpu, policy=policy, dict_slack_pct=CODINGS[coding][0], escapes=CODINGS[coding][1])
     for t in gpu.values():
         t.zero_()
     with pytest.raises(RuntimeError, match="checksum"):

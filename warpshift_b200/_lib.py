@@ -36,6 +36,8 @@ class BuildOptions(ctypes.Structure):
         ("dict_slack_pct", i32),
         ("encode_on_device", i32),
         ("encode_batch_bytes", u64),
+        ("escapes", i32),
+        ("reserved", i32),
     ]
 
 

@@ -348,6 +348,65 @@ __device__ __forceinline__ void check_dict(uint32_t& xa, uint32_t& xb, uint32_t&
     }                                                                   \
   }
 
+// Escape list of a dictionary block (WS_FLAG_ESCAPES), read by the lane that
+// owns the listed words (8l..8l+7 of every group). Their stream symbol decodes
+// as word 0, so when the decode reaches a group that holds the lane's next
+// listed word, the listed residual is ORed into the (zero) decoded half before
+// the apply: the word is written once, in its group's pass, and the checksum
+// covers it. `w` is the next listed word (0xFFFFFFFF when none is left).
+struct EscapeCursor {
+  const uint32_t* next = nullptr;
+  uint32_t left = 0;
+  uint32_t w = 0xFFFFFFFFu, y = 0;
+  bool bad = false;
+
+  // Reads the lane counts (global, so the latency overlaps the first ring copy)
+  // and the lane's first entry. A list that does not fit the payload is bad.
+  __device__ __forceinline__ void open(const ws_block_desc& bd, const uint8_t* __restrict__ src, uint32_t lane) {
+    const uint32_t side = (2u * bd.nwords + 15u) & ~15u;
+    bad = side + WS_ESCAPE_HEADER_BYTES > bd.clen;
+    uint32_t mine = 0, incl = 0;
+    if (!bad) mine = reinterpret_cast<const uint16_t*>(src + side)[lane];
+    incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= (uint32_t)o) incl += t;
+    }
+    const uint32_t total = __shfl_sync(0xFFFFFFFFu, incl, 31);
+    bad = __any_sync(0xFFFFFFFFu, bad) || side + WS_ESCAPE_HEADER_BYTES + 4ull * total > bd.clen;
+    if (bad) return;
+    next = reinterpret_cast<const uint32_t*>(src + side + WS_ESCAPE_HEADER_BYTES) + (incl - mine);
+    left = mine;
+    advance();
+  }
+  __device__ __forceinline__ void advance() {
+    if (left) {
+      const uint32_t e = *next++;
+      --left;
+      w = e & 0xFFFFu;
+      y = e >> 16;
+    } else {
+      w = 0xFFFFFFFFu;
+    }
+  }
+  // ORs every listed word of group g into the lane's residual pairs r0..r3.
+  __device__ __forceinline__ void patch(uint32_t g, uint32_t lane, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+    const uint32_t base = g * WS_GROUP_WORDS + lane * WS_WORDS_PER_LANE;
+    while (w < (g + 1) * WS_GROUP_WORDS) {
+      const uint32_t j = w - base;  // the lane's word j of this group; out of order or not owned: j >= 8
+      if (j < 8) {
+        const uint32_t add = y << (16u * (j & 1u));
+        if (j < 2) r0 |= add; else if (j < 4) r1 |= add; else if (j < 6) r2 |= add; else r3 |= add;
+      } else {
+        bad = true;
+      }
+      advance();
+    }
+  }
+};
+
 template <bool U16, bool REVERSE, bool DICT>
 __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t* __restrict__ src,
                           const uint32_t* __restrict__ tbl0, const uint32_t* __restrict__ tbl1, uint8_t* ring,
@@ -359,7 +418,9 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
   const uint32_t dec_groups = (W + WS_GROUP_WORDS - 1) / WS_GROUP_WORDS;
   const uint32_t groups = (n + WS_GROUP_BYTES - 1) / WS_GROUP_BYTES;
   const bool aligned = (bd.dst & 15u) == 0;
-  const uint32_t total_halves = (bd.clen + WS_RING_HALF_BYTES - 1) / WS_RING_HALF_BYTES;
+  // Only the stream goes through the ring; an escape list is read from global memory.
+  const uint32_t staged = (DICT && (bd.flags & WS_FLAG_ESCAPES)) ? min(bd.clen, (2u * bd.nwords + 15u) & ~15u) : bd.clen;
+  const uint32_t total_halves = (staged + WS_RING_HALF_BYTES - 1) / WS_RING_HALF_BYTES;
   const uint32_t ring_s = smem_addr(ring);
   const uint32_t ltm = lanemask_lt();
   const uint32_t tb0 = smem_addr(tbl0) + lane * 4u, tb1 = smem_addr(tbl1) + lane * 4u;
@@ -369,7 +430,7 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
   auto issue = [&](uint32_t k) {
     if (lane == 0 && k < total_halves) {
       const uint32_t off = k * WS_RING_HALF_BYTES;
-      const uint32_t bytes = min(WS_RING_HALF_BYTES, bd.clen - off);
+      const uint32_t bytes = min(WS_RING_HALF_BYTES, staged - off);
       const uint32_t bar = bar_base + (k & 1u) * 8u;
       if (k & 1u) {
         bulk_load(ring_s + WS_RING_HALF_BYTES, src + off, bytes, bar);
@@ -382,6 +443,8 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
   uint32_t issued = min(2u, total_halves);
   issue(0);
   issue(1);
+  EscapeCursor esc;
+  if (DICT && (bd.flags & WS_FLAG_ESCAPES)) esc.open(bd, src, lane);
   uint32_t ready = 0;
   bool ok = true;
   if (total_halves > 0) {
@@ -462,6 +525,7 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
         r3 = check_fast(xa, xb, rp, tb0, tb1, ltm);
       }
       pos += (rp - rp0) >> 1;
+      if (DICT) esc.patch(g, lane, r0, r1, r2, r3);
       uint4 v;
       if (U16) {
         v.x = u16_apply(old.x, r0, REVERSE);
@@ -515,6 +579,7 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
       }
     }
     uint32_t out[4] = {0, 0, 0, 0};
+    if (DICT && g < dec_groups) esc.patch(g, lane, r[0], r[1], r[2], r[3]);
     apply_chunk_bytes<U16, REVERSE>(dst + off, off, n, r, coded_bytes, bd.tail, out);
     ck.add(out[0], out[1], out[2], out[3]);
   }
@@ -522,9 +587,11 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
     if (lane == 0) report(res, WS_DEVERR_TIMEOUT, block);
   } else {
     const bool states_ok = __all_sync(0xFFFFFFFFu, xa == WS_RANS_L && xb == WS_RANS_L);
+    // Every listed word must have been consumed, in order, by its owner.
+    const bool escapes_ok = !DICT || !__any_sync(0xFFFFFFFFu, esc.bad || esc.w != 0xFFFFFFFFu);
     if (lane == 0) {
       if (!states_ok) report(res, WS_DEVERR_STATE, block);
-      if (pos != bd.nwords) report(res, WS_DEVERR_LENGTH, block);
+      if (pos != bd.nwords || !escapes_ok) report(res, WS_DEVERR_LENGTH, block);
     }
   }
   // Never leave a bulk copy in flight into shared memory of an exiting CTA.

@@ -5,7 +5,9 @@
 
 #include <string.h>
 
+#include <algorithm>
 #include <cmath>
+#include <numeric>
 
 namespace ws {
 
@@ -168,7 +170,7 @@ inline uint16_t residual_word(const uint8_t* base, const uint8_t* target, uint64
 // values and its estimated size is within dict_slack_pct percent of the planes'.
 template <bool U16>
 void build_candidate(const uint8_t* base, const uint8_t* target, uint64_t n, const std::vector<uint8_t>& nonzero,
-                     int dict_slack_pct, Candidate* cand) {
+                     const CodingOptions& co, Candidate* cand) {
   const uint64_t W = n / 2;  // coded words; an odd last byte is carried raw in the block's tail field
   uint64_t counts[2][256];
   memset(counts, 0, sizeof(counts));
@@ -196,13 +198,15 @@ void build_candidate(const uint8_t* base, const uint8_t* target, uint64_t n, con
       wcounts.push_back(word_counts[v]);
     }
   CodingTables ct;
-  choose_coding(counts, words, wcounts, words.size() > 255, coded_blocks, dict_slack_pct, &ct);
+  choose_coding(counts, words, wcounts, words.size() > 255, coded_blocks, co, &ct);
   const bool use_dict = ct.dict;
+  const uint8_t esc = (uint8_t)ct.words.size();  // the escape symbol (when ct.escape)
   std::vector<uint8_t> index_of;
   if (use_dict) {
-    index_of.assign(65536, 0);
+    index_of.assign(65536, ct.escape ? esc : 0);
     for (size_t i = 0; i < ct.words.size(); ++i) index_of[ct.words[i]] = (uint8_t)i;
   }
+  std::vector<uint32_t> lanes[WS_LANES];
   memcpy(cand->table, ct.entries, sizeof(cand->table));
   cand->size = 1024;  // compact per-packet tables (frequencies, and the dictionary words)
   const Schedule sc{use_dict};
@@ -219,14 +223,22 @@ void build_candidate(const uint8_t* base, const uint8_t* target, uint64_t n, con
     const uint32_t wb = blk.nbytes / 2;
     const uint8_t* bb = base + blk.offset;
     const uint8_t* tb = target + blk.offset;
+    for (auto& l : lanes) l.clear();
     for (uint32_t w = 0; w < wb; ++w) {
       const uint16_t v = residual_word<U16>(bb, tb, w);
       if (use_dict) {
         s0[w] = s1[w] = index_of[v];
+        if (ct.escape && index_of[v] == esc)
+          lanes[(w % WS_GROUP_WORDS) / WS_WORDS_PER_LANE].push_back(w | ((uint32_t)v << 16));
       } else {
         s0[w] = (uint8_t)(v & 0xFF);
         s1[w] = (uint8_t)(v >> 8);
       }
+    }
+    size_t most = 0, escaped = 0;
+    for (const auto& l : lanes) {
+      most = std::max(most, l.size());
+      escaped += l.size();
     }
     if (blk.nbytes & 1u) {
       blk.flags |= WS_FLAG_ODD_TAIL;
@@ -235,8 +247,12 @@ void build_candidate(const uint8_t* base, const uint8_t* target, uint64_t n, con
     const uint8_t* sym[2] = {s0.data(), s1.data()};
     encode_ans_block(sc, sym, wb, freq, cdf, &blk.payload, &blk.nwords);
     blk.kind = use_dict ? (U16 ? WS_KIND_DICT_U16 : WS_KIND_DICT_XOR) : (U16 ? WS_KIND_ANS_U16 : WS_KIND_ANS_XOR);
+    if (escaped) {
+      blk.flags |= WS_FLAG_ESCAPES;
+      append_escapes(lanes, &blk.payload);
+    }
     const uint32_t raw = round_up16(blk.nbytes);
-    if (blk.payload.size() >= raw) {  // incompressible block: carry its XOR bytes raw
+    if (blk.payload.size() >= raw || most > WS_ESCAPE_LANE_MAX) {  // incompressible, or too many escapes: raw XOR
       blk.kind = WS_KIND_RAW;
       blk.flags = 0;
       blk.tail = 0;
@@ -314,35 +330,108 @@ void build_slot_entries(const uint32_t freqs[256], uint32_t entries[256]) {
   for (; slot < 256; ++slot) entries[slot] = 0;  // only reachable for an empty table
 }
 
+namespace {
+
+// Dictionary tables from symbol counts (symbol i = words[i], plus the escape
+// symbol words.size() when `escape`); returns the estimated payload bytes.
+double dict_tables(const std::vector<uint16_t>& words, const uint64_t* sym_counts, bool escape, uint64_t escaped,
+                   uint32_t coded_blocks, CodingTables* out) {
+  uint64_t dcounts[256];
+  uint32_t dict_freq[256];
+  memset(dcounts, 0, sizeof(dcounts));
+  const size_t nsym = words.size() + (escape ? 1 : 0);
+  for (size_t i = 0; i < nsym; ++i) dcounts[i] = sym_counts[i];
+  quantize_frequencies(dcounts, dict_freq);
+  double est = estimate_bytes(dcounts, dict_freq, 256, coded_blocks);
+  if (escape) est += 4.0 * (double)escaped + (double)coded_blocks * WS_ESCAPE_HEADER_BYTES;
+  if (out) {
+    out->dict = true;
+    out->escape = escape;
+    out->words = words;
+    uint32_t c = 0, slot = 0;
+    for (uint32_t i = 0; i < 256; ++i) {
+      out->freq[0][i] = out->freq[1][i] = dict_freq[i];
+      out->cdf[0][i] = out->cdf[1][i] = c;
+      c += dict_freq[i];
+    }
+    memset(out->entries, 0, sizeof(out->entries));
+    for (size_t i = 0; i < nsym; ++i) {
+      const uint16_t word = i < words.size() ? words[i] : 0;  // the escape symbol decodes as 0: no change
+      for (uint32_t k = 0; k < dict_freq[i]; ++k, ++slot) out->entries[slot] = WS_DICT_ENTRY(k, word, dict_freq[i]);
+    }
+  }
+  return est;
+}
+
+}  // namespace
+
 void choose_coding(const uint64_t counts[2][256], const std::vector<uint16_t>& words,
-                   const std::vector<uint64_t>& word_counts, bool many_words, uint32_t coded_blocks, int dict_slack_pct,
-                   CodingTables* out) {
+                   const std::vector<uint64_t>& word_counts, bool many_words, uint32_t coded_blocks,
+                   const CodingOptions& co, CodingTables* out) {
   PlaneTables t;
   uint32_t plane_entries[512];
   tables_from_counts(counts, &t, plane_entries);
   const double planes_est = estimate_bytes(counts[0], t.freq[0], 256, coded_blocks) +
                             estimate_bytes(counts[1], t.freq[1], 256, 0);
   out->dict = false;
+  out->escape = false;
   out->words.clear();
-  if (dict_slack_pct >= 0 && !many_words && words.size() >= 2 && words.size() <= 255) {
-    uint64_t dcounts[256];
-    uint32_t dict_freq[256];
-    memset(dcounts, 0, sizeof(dcounts));
-    for (size_t i = 0; i < words.size(); ++i) dcounts[i] = word_counts[i];
-    quantize_frequencies(dcounts, dict_freq);
-    const double dict_est = estimate_bytes(dcounts, dict_freq, 256, coded_blocks);
-    if (dict_est <= planes_est * (1.0 + dict_slack_pct / 100.0)) {
-      out->dict = true;
-      out->words = words;
-      uint32_t c = 0, slot = 0;
-      for (uint32_t i = 0; i < 256; ++i) {
-        out->freq[0][i] = out->freq[1][i] = dict_freq[i];
-        out->cdf[0][i] = out->cdf[1][i] = c;
-        c += dict_freq[i];
+  if (co.dict_slack_pct >= 0 && !many_words && words.size() >= 2 && words.size() <= 255) {
+    // Plain dictionary: every distinct word is a symbol.
+    double best = dict_tables(words, word_counts.data(), false, 0, coded_blocks, nullptr);
+    size_t best_k = words.size();
+    // Dictionaries with escapes: the K most frequent words (ties: smaller word
+    // first) are symbols, every other word is escaped.
+    if (co.escapes >= 0) {
+      std::vector<uint32_t> order(words.size());
+      std::iota(order.begin(), order.end(), 0u);
+      std::stable_sort(order.begin(), order.end(),
+                       [&](uint32_t x, uint32_t y) { return word_counts[x] > word_counts[y]; });
+      const uint64_t total = std::accumulate(word_counts.begin(), word_counts.end(), (uint64_t)0);
+      bool first = true;
+      for (size_t k : {8, 12, 16, 24, 32, 48, 64, 96, 128, 192}) {
+        if (k >= words.size()) break;
+        uint64_t escaped = 0;
+        for (size_t r = k; r < order.size(); ++r) escaped += word_counts[order[r]];
+        if (escaped * 100 > total) continue;  // keep the per-lane lists short
+        std::vector<uint32_t> kept(order.begin(), order.begin() + k);
+        std::sort(kept.begin(), kept.end());
+        std::vector<uint16_t> kw;
+        std::vector<uint64_t> kc;
+        for (uint32_t i : kept) {
+          kw.push_back(words[i]);
+          kc.push_back(word_counts[i]);
+        }
+        kc.push_back(escaped);
+        const double est = dict_tables(kw, kc.data(), true, escaped, coded_blocks, nullptr);
+        if (est < best || (co.escapes > 0 && first)) {
+          best = est;
+          best_k = k;
+          first = false;
+        }
       }
-      memset(out->entries, 0, sizeof(out->entries));
-      for (size_t i = 0; i < words.size(); ++i)
-        for (uint32_t k = 0; k < dict_freq[i]; ++k, ++slot) out->entries[slot] = WS_DICT_ENTRY(k, words[i], dict_freq[i]);
+    }
+    if (best <= planes_est * (1.0 + co.dict_slack_pct / 100.0) || (co.escapes > 0 && best_k < words.size())) {
+      if (best_k == words.size()) {
+        dict_tables(words, word_counts.data(), false, 0, coded_blocks, out);
+      } else {
+        std::vector<uint32_t> order(words.size());
+        std::iota(order.begin(), order.end(), 0u);
+        std::stable_sort(order.begin(), order.end(),
+                         [&](uint32_t x, uint32_t y) { return word_counts[x] > word_counts[y]; });
+        uint64_t escaped = 0;
+        for (size_t r = best_k; r < order.size(); ++r) escaped += word_counts[order[r]];
+        std::vector<uint32_t> kept(order.begin(), order.begin() + best_k);
+        std::sort(kept.begin(), kept.end());
+        std::vector<uint16_t> kw;
+        std::vector<uint64_t> kc;
+        for (uint32_t i : kept) {
+          kw.push_back(words[i]);
+          kc.push_back(word_counts[i]);
+        }
+        kc.push_back(escaped);
+        dict_tables(kw, kc.data(), true, escaped, coded_blocks, out);
+      }
       return;
     }
   }
@@ -381,8 +470,25 @@ uint64_t block_lane_sum(const uint8_t* bytes, uint32_t n) {
   return sum;
 }
 
+void append_escapes(const std::vector<uint32_t> lanes[WS_LANES], std::vector<uint8_t>* payload) {
+  size_t at = payload->size();
+  size_t total = 0;
+  for (uint32_t l = 0; l < WS_LANES; ++l) total += lanes[l].size();
+  payload->resize(round_up16((uint32_t)(at + WS_ESCAPE_HEADER_BYTES + 4 * total)), 0);
+  uint8_t* p = payload->data() + at;
+  for (uint32_t l = 0; l < WS_LANES; ++l) {
+    const uint16_t c = (uint16_t)lanes[l].size();
+    memcpy(p + 2 * l, &c, 2);
+  }
+  p += WS_ESCAPE_HEADER_BYTES;
+  for (uint32_t l = 0; l < WS_LANES; ++l) {
+    memcpy(p, lanes[l].data(), 4 * lanes[l].size());
+    p += 4 * lanes[l].size();
+  }
+}
+
 void encode_packet(const uint8_t* base, const uint8_t* target, uint64_t n, bool is_bf16, int policy,
-                   int dict_slack_pct, EncodedPacket* out) {
+                   const CodingOptions& co, EncodedPacket* out) {
   out->nbytes = n;
   out->blocks.clear();
   out->zero_block_bytes = 0;
@@ -408,7 +514,7 @@ void encode_packet(const uint8_t* base, const uint8_t* target, uint64_t n, bool 
   const bool try_u16 = big && is_bf16 && (n % 2 == 0) && policy != 1;
   if (try_xor) {
     Candidate c;
-    build_candidate<false>(base, target, n, nonzero, dict_slack_pct, &c);
+    build_candidate<false>(base, target, n, nonzero, co, &c);
     if (c.size < best) {  // delta.py:188-189: strictly smaller replaces raw
       best = c.size;
       mode = (n % 2 == 0) ? WS_MODE_XOR_GROUP2_ANS : WS_MODE_XOR_ANS;
@@ -417,7 +523,7 @@ void encode_packet(const uint8_t* base, const uint8_t* target, uint64_t n, bool 
   }
   if (try_u16) {
     Candidate c;
-    build_candidate<true>(base, target, n, nonzero, dict_slack_pct, &c);
+    build_candidate<true>(base, target, n, nonzero, co, &c);
     if (c.size < best) {  // delta.py:192-193: strictly smaller than the current best
       best = c.size;
       mode = WS_MODE_U16_ANS;

@@ -30,22 +30,33 @@ struct EncodedPacket {
   std::vector<EncodedBlock> blocks;  // non-zero blocks in order
 };
 
+// Coding choices of a plan (ws_build_options).
+struct CodingOptions {
+  int dict_slack_pct = 6;  // word dictionary when within this many % of the byte planes' size; < 0: never
+  int escapes = 0;         // dictionary with escapes: 0 when smaller, < 0 never, > 0 whenever eligible
+};
+
 // Tables of one packet coding: byte planes (two tables) or word dictionary
-// (one table for both states, whose symbols index `words`).
+// (one table for both states, whose symbols index `words`; with `escape`, the
+// extra symbol words.size() stands for every other word, decoded as word 0 and
+// listed per block after the stream, see WS_FLAG_ESCAPES).
 struct CodingTables {
   bool dict = false;
+  bool escape = false;
   uint32_t entries[512];          // slot entries as the kernel reads them
   uint32_t freq[2][256], cdf[2][256];
-  std::vector<uint16_t> words;    // dictionary: word of each symbol, increasing
+  std::vector<uint16_t> words;    // dictionary: word of each kept symbol, increasing
 };
 
 // Builds the byte-plane tables from `counts` (plane histograms over the coded
 // words) and switches to the word dictionary when the packet has 2..255
 // distinct words (`words` increasing, `word_counts` aligned; many_words = more
 // than 255) and its estimated size is within dict_slack_pct % of the planes'.
+// The dictionary keeps all words, or (escapes) only the most frequent ones when
+// that is estimated smaller and the escaped words are at most 1 % of the words.
 void choose_coding(const uint64_t counts[2][256], const std::vector<uint16_t>& words,
-                   const std::vector<uint64_t>& word_counts, bool many_words, uint32_t coded_blocks, int dict_slack_pct,
-                   CodingTables* out);
+                   const std::vector<uint64_t>& word_counts, bool many_words, uint32_t coded_blocks,
+                   const CodingOptions& co, CodingTables* out);
 
 // Quantise symbol counts to frequencies summing to WS_PROB_SCALE; every symbol
 // with a non-zero count gets frequency >= 1. Greedy fix-up minimising code length.
@@ -58,10 +69,12 @@ void build_slot_entries(const uint32_t freqs[256], uint32_t entries[256]);
 void u16_residual_reference(const uint8_t* base, const uint8_t* target, uint64_t nbytes, uint8_t* out);
 
 // Encode one packet (<= WS_PACKET_BYTES) following delta.py:176-194 with our codec.
-// dict_slack_pct: use the word-dictionary coding when its estimated size is at
-// most this many percent above the byte-plane coding (negative: never).
 void encode_packet(const uint8_t* base, const uint8_t* target, uint64_t nbytes, bool is_bf16, int policy,
-                   int dict_slack_pct, EncodedPacket* out);
+                   const CodingOptions& co, EncodedPacket* out);
+
+// Appends a block's escape list (WS_FLAG_ESCAPES layout) to a payload whose
+// stream part is already padded to 16 bytes. lanes[l] = lane l's entries.
+void append_escapes(const std::vector<uint32_t> lanes[WS_LANES], std::vector<uint8_t>* payload);
 
 // Checksum lane sum of `n` bytes (one block) as defined in ws_format.h.
 uint64_t block_lane_sum(const uint8_t* bytes, uint32_t n);

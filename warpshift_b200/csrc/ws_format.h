@@ -57,6 +57,18 @@ enum ws_kind {
   WS_KIND_DICT_U16 = 4   // word dictionary, wrapping u16 apply
 };
 #define WS_FLAG_ODD_TAIL 1u  // block's last byte (odd packet size) is not coded; its XOR value is `tail`
+// Word-dictionary block with escapes: the packet's dictionary keeps its most
+// frequent words plus one escape symbol whose word is 0 (no change in either
+// apply), and every escaped word of the block is listed after the stream. The
+// list starts at byte align16(2 * nwords) of the payload: uint16 count[32] (the
+// entries of each lane, lane l owning words 8l..8l+7 of every 256-word group),
+// then the entries grouped by lane in lane order, each uint32 = word index in
+// the block (bits 0-15) | coded residual word (bits 16-31), increasing index
+// within a lane; zero-padded to 16 bytes. After decoding, each lane applies its
+// own entries and corrects its checksum sums.
+#define WS_FLAG_ESCAPES 2u
+#define WS_ESCAPE_LANE_MAX 64u  // entries per lane at most; an encoder codes a block with more as RAW
+#define WS_ESCAPE_HEADER_BYTES 64u
 
 // Device-side errors reported through ws_device_result.errors.
 #define WS_DEVERR_STATE 1u     // final rANS state != WS_RANS_L

@@ -70,6 +70,7 @@ struct EncodeJob {  // one block coded with one candidate
   uint32_t table;     // index into the batch's encode tables
   uint32_t dict;      // 1: word dictionary, 0: byte planes
   uint32_t u16;       // 1: U16 residual words, 0: XOR words
+  uint32_t esc;       // the dictionary's escape symbol, or ~0u without escapes
 };
 
 struct EncTable {  // per candidate coding: per state, per symbol
@@ -81,7 +82,7 @@ struct CompactJob {
   uint32_t block;      // BlockJob index
   uint32_t encode;     // EncodeJob index (source of an ANS payload), or ~0u for raw
   uint32_t nwords;     // ANS halfwords incl. header
-  uint32_t pad;
+  uint32_t escapes;    // escape entries listed after the stream (0: no list)
   uint64_t dst;        // byte offset in the output buffer
 };
 
@@ -89,6 +90,29 @@ __device__ __forceinline__ uint16_t u16_word(uint16_t b, uint16_t t) {
   const int32_t d = (int32_t)(int16_t)(uint16_t)(t - b);
   const uint32_t z = ((uint32_t)(d * 2) ^ (uint32_t)(d >> 15)) & 0xFFFFu;
   return (uint16_t)((z >> 1) | ((z & 1u) << 15));
+}
+
+// The lane's 8 residual words starting at word w0 of the block (0 past W).
+__device__ __forceinline__ void load_words(const BlockJob& blk, uint32_t w0, uint32_t W, bool aligned, bool u16,
+                                           uint16_t v[8]) {
+  if (w0 + 8 <= W && aligned) {
+    uint4 av = *reinterpret_cast<const uint4*>(blk.base + 2 * w0);
+    uint4 tv = *reinterpret_cast<const uint4*>(blk.target + 2 * w0);
+    const uint16_t* a16 = reinterpret_cast<const uint16_t*>(&av);
+    const uint16_t* t16 = reinterpret_cast<const uint16_t*>(&tv);
+#pragma unroll
+    for (uint32_t q = 0; q < 8; ++q) v[q] = u16 ? u16_word(a16[q], t16[q]) : (uint16_t)(a16[q] ^ t16[q]);
+  } else {
+#pragma unroll
+    for (uint32_t q = 0; q < 8; ++q) {
+      v[q] = 0;
+      if (w0 + q < W) {
+        const uint16_t a16 = (uint16_t)(blk.base[2 * (w0 + q)] | (blk.base[2 * (w0 + q) + 1] << 8));
+        const uint16_t t16 = (uint16_t)(blk.target[2 * (w0 + q)] | (blk.target[2 * (w0 + q) + 1] << 8));
+        v[q] = u16 ? u16_word(a16, t16) : (uint16_t)(a16 ^ t16);
+      }
+    }
+  }
 }
 
 __device__ __forceinline__ uint32_t word_hash(uint32_t w, uint32_t bits) { return (w * 0x9E3779B1u) >> (32 - bits); }
@@ -254,7 +278,8 @@ __global__ void __launch_bounds__(kEncWarps * 32) encode_kernel(const BlockJob* 
                                                                 const EncodeJob* __restrict__ jobs, uint32_t njobs,
                                                                 const EncTable* __restrict__ tables,
                                                                 const uint8_t* const* __restrict__ dict_index,
-                                                                uint16_t* out, uint32_t* nwords_out) {
+                                                                uint16_t* out, uint32_t* nwords_out,
+                                                                uint32_t* side_out, uint32_t* side_count) {
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const uint32_t j = blockIdx.x * kEncWarps + warp;
   if (j >= njobs) return;
@@ -270,28 +295,28 @@ __global__ void __launch_bounds__(kEncWarps * 32) encode_kernel(const BlockJob* 
   const bool aligned = (((uintptr_t)blk.base | (uintptr_t)blk.target) & 15u) == 0;
   uint32_t x[2] = {WS_RANS_L, WS_RANS_L};
   uint32_t cursor = kOutHalfwords;
+  if (job.esc != ~0u) {
+    // Escape list of this lane: its words coded as the escape symbol, in
+    // increasing word order (at most WS_ESCAPE_LANE_MAX stored; the count is exact).
+    uint32_t* mine = side_out + ((uint64_t)j * WS_LANES + lane) * WS_ESCAPE_LANE_MAX;
+    uint32_t count = 0;
+    for (uint32_t g = 0; g < groups; ++g) {
+      const uint32_t w0 = g * WS_GROUP_WORDS + lane * WS_WORDS_PER_LANE;
+      uint16_t v[8];
+      load_words(blk, w0, W, aligned, job.u16 != 0, v);
+      for (uint32_t q = 0; q < 8; ++q)
+        if (w0 + q < W && idx[v[q]] == job.esc) {
+          if (count < WS_ESCAPE_LANE_MAX) mine[count] = (w0 + q) | ((uint32_t)v[q] << 16);
+          ++count;
+        }
+    }
+    side_count[(uint64_t)j * WS_LANES + lane] = count;
+  }
   for (uint32_t g = groups; g-- > 0;) {
     // The lane's 8 residual words of this group and their symbols per state.
     const uint32_t w0 = g * WS_GROUP_WORDS + lane * WS_WORDS_PER_LANE;
     uint16_t v[8];
-    if (w0 + 8 <= W && aligned) {
-      uint4 av = *reinterpret_cast<const uint4*>(blk.base + 2 * w0);
-      uint4 tv = *reinterpret_cast<const uint4*>(blk.target + 2 * w0);
-      const uint16_t* a16 = reinterpret_cast<const uint16_t*>(&av);
-      const uint16_t* t16 = reinterpret_cast<const uint16_t*>(&tv);
-#pragma unroll
-      for (uint32_t q = 0; q < 8; ++q) v[q] = job.u16 ? u16_word(a16[q], t16[q]) : (uint16_t)(a16[q] ^ t16[q]);
-    } else {
-#pragma unroll
-      for (uint32_t q = 0; q < 8; ++q) {
-        v[q] = 0;
-        if (w0 + q < W) {
-          const uint16_t a16 = (uint16_t)(blk.base[2 * (w0 + q)] | (blk.base[2 * (w0 + q) + 1] << 8));
-          const uint16_t t16 = (uint16_t)(blk.target[2 * (w0 + q)] | (blk.target[2 * (w0 + q) + 1] << 8));
-          v[q] = job.u16 ? u16_word(a16, t16) : (uint16_t)(a16 ^ t16);
-        }
-      }
-    }
+    load_words(blk, w0, W, aligned, job.u16 != 0, v);
     for (uint32_t c = cpg; c-- > 0;) {
       uint32_t sa[2], sb[2];
       bool pa[2], pb[2];
@@ -360,7 +385,8 @@ __global__ void __launch_bounds__(kEncWarps * 32) encode_kernel(const BlockJob* 
 // Packs one block's payload (ANS header + stream, or raw XOR bytes) at dst,
 // zero-padded to 16 bytes.
 __global__ void compact_kernel(const CompactJob* __restrict__ jobs, const BlockJob* __restrict__ blocks,
-                               const uint16_t* __restrict__ enc_out, uint8_t* out) {
+                               const uint16_t* __restrict__ enc_out, const uint32_t* __restrict__ side_out,
+                               const uint32_t* __restrict__ side_count, uint8_t* out) {
   const CompactJob job = jobs[blockIdx.x];
   const BlockJob blk = blocks[job.block];
   uint8_t* d = out + job.dst;
@@ -382,6 +408,27 @@ __global__ void compact_kernel(const CompactJob* __restrict__ jobs, const BlockJ
       v = src[first + (i - WS_HEADER_HALFWORDS)];
     d16[i] = v;
   }
+  if (job.escapes == 0) return;
+  // Escape list (WS_FLAG_ESCAPES layout): lane counts, entries by lane, zero padding.
+  __shared__ uint32_t start[WS_LANES + 1];
+  const uint32_t* cnt = side_count + (uint64_t)job.encode * WS_LANES;
+  if (threadIdx.x == 0) {
+    start[0] = 0;
+    for (uint32_t l = 0; l < WS_LANES; ++l) start[l + 1] = start[l] + cnt[l];
+  }
+  __syncthreads();
+  uint8_t* side = d + 2 * padded_hw;
+  uint16_t* head = reinterpret_cast<uint16_t*>(side);
+  if (threadIdx.x < WS_LANES) head[threadIdx.x] = (uint16_t)cnt[threadIdx.x];
+  uint32_t* ent = reinterpret_cast<uint32_t*>(side + WS_ESCAPE_HEADER_BYTES);
+  const uint32_t* lanes = side_out + (uint64_t)job.encode * WS_LANES * WS_ESCAPE_LANE_MAX;
+  for (uint32_t e = threadIdx.x; e < job.escapes; e += blockDim.x) {
+    uint32_t l = 0;
+    while (start[l + 1] <= e) ++l;
+    ent[e] = lanes[l * WS_ESCAPE_LANE_MAX + (e - start[l])];
+  }
+  const uint32_t used = WS_ESCAPE_HEADER_BYTES + 4 * job.escapes, padded = (used + 15) & ~15u;
+  for (uint32_t i = used + threadIdx.x; i < padded; i += blockDim.x) side[i] = 0;
 }
 
 template <class T>
@@ -614,7 +661,7 @@ void free_host_chunk(const ArenaChunk& c) {
     }                                                                                \
   } while (0)
 
-bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, int dict_slack_pct,
+bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, const CodingOptions& co,
                         uint64_t batch_bytes, int threads, bool pin, cudaStream_t stream,
                         std::vector<EncodedPacket>* out, std::vector<ArenaChunk>* chunks, std::string* err,
                         bool* device_oom) {
@@ -642,6 +689,7 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
   DeviceBuffer<uint32_t> d_nwords;
   DeviceBuffer<CompactJob> d_compact;
   DeviceBuffer<uint16_t> d_words;
+  DeviceBuffer<uint32_t> d_side, d_side_count;
   // Batches: consecutive packets up to batch_bytes of weights; packets start
   // 256-byte aligned in the device copy of A.
   std::vector<std::pair<size_t, size_t>> ranges;
@@ -725,6 +773,8 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
     std::vector<Cand> cand(np * 2);
     std::vector<EncTable> tables;
     std::vector<std::vector<uint16_t>> dict_words;
+    std::vector<int> dict_esc;  // escape symbol of each dictionary, or -1
+    bool any_escape = false;
     std::vector<int> dict_of_table;
     std::vector<EncodeJob> jobs;
     std::vector<std::vector<uint32_t>> job_of(np * 2);
@@ -774,7 +824,7 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
           wcounts.push_back(pr.second);
         }
         CodingTables& ct = coding[2 * i + c];
-        choose_coding(counts, words, wcounts, many || words.size() > 255, coded, dict_slack_pct, &ct);
+        choose_coding(counts, words, wcounts, many || words.size() > 255, coded, co, &ct);
         Cand& cd = cand[2 * i + c];
         cd.table = (int)tables.size();
         cd.dict = ct.dict;
@@ -782,11 +832,16 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
         fill_enc_table(ct, &et);
         tables.push_back(et);
         dict_of_table.push_back(ct.dict ? (int)dict_words.size() : -1);
-        if (ct.dict) dict_words.push_back(ct.words);
+        if (ct.dict) {
+          dict_words.push_back(ct.words);
+          dict_esc.push_back(ct.escape ? (int)ct.words.size() : -1);
+        }
+        const uint32_t esc = ct.escape ? (uint32_t)ct.words.size() : ~0u;
+        any_escape |= ct.escape;
         for (uint32_t b = packet_first_block[i]; b < packet_first_block[i + 1]; ++b) {
           if (!bstats[b].nonzero) continue;
           job_of[2 * i + c].push_back((uint32_t)jobs.size());
-          jobs.push_back(EncodeJob{b, (uint32_t)cd.table, ct.dict ? 1u : 0u, (uint32_t)c});
+          jobs.push_back(EncodeJob{b, (uint32_t)cd.table, ct.dict ? 1u : 0u, (uint32_t)c, esc});
         }
       }
     }
@@ -794,6 +849,21 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
     t0 = now();
     // Encode every candidate block.
     std::vector<uint32_t> nwords(jobs.size());
+    std::vector<uint32_t> side_count;
+    // Payload of job jj when coded: stream (+ escape list); `ok` is false when a
+    // lane has more escapes than a list holds (the block is then coded raw).
+    auto coded_size = [&](uint32_t jj, bool* ok, uint32_t* escapes) {
+      uint32_t size = (2 * nwords[jj] + 15) & ~15u, total = 0, most = 0;
+      if (jobs[jj].esc != ~0u)
+        for (uint32_t l = 0; l < WS_LANES; ++l) {
+          total += side_count[(size_t)jj * WS_LANES + l];
+          most = std::max(most, side_count[(size_t)jj * WS_LANES + l]);
+        }
+      if (total) size += (WS_ESCAPE_HEADER_BYTES + 4 * total + 15) & ~15u;
+      *ok = most <= WS_ESCAPE_LANE_MAX;
+      *escapes = total;
+      return size;
+    };
     if (!jobs.empty()) {
       WS_GPU_TRY(d_tables.ensure(tables.size()));
       WS_GPU_TRY(cudaMemcpyAsync(d_tables.ptr, tables.data(), tables.size() * sizeof(EncTable), cudaMemcpyHostToDevice, stream));
@@ -806,6 +876,8 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
         index_ptrs[t] = d_index.ptr + (size_t)d * 65536;
         uint16_t* dw = d_words.ptr + (size_t)d * 256;
         WS_GPU_TRY(cudaMemcpyAsync(dw, dict_words[d].data(), dict_words[d].size() * 2, cudaMemcpyHostToDevice, stream));
+        // Words outside the dictionary map to its escape symbol (never looked up without escapes).
+        WS_GPU_TRY(cudaMemsetAsync(d_index.ptr + (size_t)d * 65536, dict_esc[d] >= 0 ? dict_esc[d] : 0, 65536, stream));
         dict_index_kernel<<<1, 256, 0, stream>>>(dw, (uint32_t)dict_words[d].size(), d_index.ptr + (size_t)d * 65536);
         WS_GPU_TRY(cudaGetLastError());
       }
@@ -815,11 +887,19 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
       WS_GPU_TRY(cudaMemcpyAsync(d_jobs.ptr, jobs.data(), jobs.size() * sizeof(EncodeJob), cudaMemcpyHostToDevice, stream));
       WS_GPU_TRY(d_enc.ensure(jobs.size() * (size_t)kOutHalfwords));
       WS_GPU_TRY(d_nwords.ensure(jobs.size()));
+      WS_GPU_TRY(d_side.ensure(any_escape ? jobs.size() * WS_LANES * WS_ESCAPE_LANE_MAX : 1));
+      WS_GPU_TRY(d_side_count.ensure(any_escape ? jobs.size() * WS_LANES : 1));
       const unsigned grid = (unsigned)((jobs.size() + kEncWarps - 1) / kEncWarps);
       encode_kernel<<<grid, kEncWarps * 32, 0, stream>>>(d_blocks.ptr, d_jobs.ptr, (uint32_t)jobs.size(), d_tables.ptr,
-                                                         d_index_ptrs.ptr, d_enc.ptr, d_nwords.ptr);
+                                                         d_index_ptrs.ptr, d_enc.ptr, d_nwords.ptr, d_side.ptr,
+                                                         d_side_count.ptr);
       WS_GPU_TRY(cudaGetLastError());
       WS_GPU_TRY(cudaMemcpyAsync(nwords.data(), d_nwords.ptr, jobs.size() * 4, cudaMemcpyDeviceToHost, stream));
+      if (any_escape) {
+        side_count.resize(jobs.size() * WS_LANES);
+        WS_GPU_TRY(cudaMemcpyAsync(side_count.data(), d_side_count.ptr, side_count.size() * 4, cudaMemcpyDeviceToHost,
+                                   stream));
+      }
       WS_GPU_TRY(cudaStreamSynchronize(stream));
     }
     t_encode += secs(t0, now());
@@ -837,9 +917,11 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
         if (cand[2 * i + c].table < 0) continue;
         uint64_t size = 1024;
         for (uint32_t jj : job_of[2 * i + c]) {
-          const uint32_t ans = (2 * nwords[jj] + 15) & ~15u;
+          bool ok;
+          uint32_t esc_n;
+          const uint32_t ans = coded_size(jj, &ok, &esc_n);
           const uint32_t raw = (blocks[jobs[jj].block].nbytes + 15) & ~15u;
-          size += ans < raw ? ans : raw;
+          size += ok && ans < raw ? ans : raw;
         }
         if (size < best) {
           best = size;
@@ -870,8 +952,10 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
         uint32_t size = raw;
         if (best_c >= 0) {
           const uint32_t jj = job_of[2 * i + best_c][jpos];
-          const uint32_t ans = (2 * nwords[jj] + 15) & ~15u;
-          if (ans < raw) {
+          bool ok;
+          uint32_t esc_n;
+          const uint32_t ans = coded_size(jj, &ok, &esc_n);
+          if (ok && ans < raw) {
             const bool dict = cand[2 * i + best_c].dict;
             blk.kind = best_c == 1 ? (dict ? WS_KIND_DICT_U16 : WS_KIND_ANS_U16)
                                    : (dict ? WS_KIND_DICT_XOR : WS_KIND_ANS_XOR);
@@ -880,8 +964,10 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
               blk.flags = WS_FLAG_ODD_TAIL;
               blk.tail = (uint8_t)bstats[b].tail;
             }
+            if (esc_n) blk.flags |= WS_FLAG_ESCAPES;
             cj.encode = jj;
             cj.nwords = nwords[jj];
+            cj.escapes = esc_n;
             size = ans;
           }
         }
@@ -897,7 +983,8 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
       WS_GPU_TRY(d_compact.ensure(compact.size()));
       WS_GPU_TRY(d_payload.ensure(out_bytes));
       WS_GPU_TRY(cudaMemcpyAsync(d_compact.ptr, compact.data(), compact.size() * sizeof(CompactJob), cudaMemcpyHostToDevice, stream));
-      compact_kernel<<<(unsigned)compact.size(), 256, 0, stream>>>(d_compact.ptr, d_blocks.ptr, d_enc.ptr, d_payload.ptr);
+      compact_kernel<<<(unsigned)compact.size(), 256, 0, stream>>>(d_compact.ptr, d_blocks.ptr, d_enc.ptr, d_side.ptr,
+                                                                   d_side_count.ptr, d_payload.ptr);
       WS_GPU_TRY(cudaGetLastError());
       // The batch's payloads become one arena chunk (arena order is packet, block order).
       ArenaChunk ch;

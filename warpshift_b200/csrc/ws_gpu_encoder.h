@@ -42,7 +42,7 @@ void free_host_chunk(const ArenaChunk& chunk);
 // threads. Returns false with *err set on a CUDA or allocation error;
 // *device_oom tells whether a device allocation was what failed (the caller may
 // retry with smaller batches).
-bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, int dict_slack_pct,
+bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, const CodingOptions& co,
                         uint64_t batch_bytes, int threads, bool pin, cudaStream_t stream,
                         std::vector<EncodedPacket>* out, std::vector<ArenaChunk>* chunks, std::string* err,
                         bool* device_oom);

@@ -57,6 +57,13 @@ int default_threads() {
   return n ? (int)n : 1;
 }
 
+ws::CodingOptions coding_options(const ws_build_options& o) {
+  ws::CodingOptions co;
+  co.dict_slack_pct = o.dict_slack_pct;
+  co.escapes = o.escapes;
+  return co;
+}
+
 // Run fn(i) for i in [0, n) on `threads` threads.
 template <class F>
 void parallel_for(uint64_t n, int threads, F fn) {
@@ -150,7 +157,7 @@ int encode_all(const ws_tensor_desc* tensors, const std::vector<PacketRef>& pack
     for (uint64_t batch = o.encode_batch_bytes ? o.encode_batch_bytes : (512ull << 20);; batch /= 4) {
       std::string err;
       bool oom = false;
-      if (ws::gpu_encode_packets(in, o.policy, o.dict_slack_pct, batch, threads, o.pin_arena != 0, stream, out,
+      if (ws::gpu_encode_packets(in, o.policy, coding_options(o), batch, threads, o.pin_arena != 0, stream, out,
                                  chunks, &err, &oom)) {
         *external = true;
         return WS_OK;
@@ -167,7 +174,7 @@ int encode_all(const ws_tensor_desc* tensors, const std::vector<PacketRef>& pack
       const PacketRef& pr = packets[i];
       const ws_tensor_desc& t = tensors[pr.tensor];
       ws::encode_packet((const uint8_t*)t.base + pr.offset, (const uint8_t*)t.target + pr.offset, pr.nbytes,
-                        t.is_bf16 != 0, o.policy, o.dict_slack_pct, &(*out)[i]);
+                        t.is_bf16 != 0, o.policy, coding_options(o), &(*out)[i]);
     });
     return WS_OK;
   }
@@ -206,7 +213,7 @@ int encode_all(const ws_tensor_desc* tensors, const std::vector<PacketRef>& pack
         worker_error = true;
       } else {
         ws::encode_packet((const uint8_t*)t.base + pr.offset, bufs[job.second], pr.nbytes, t.is_bf16 != 0,
-                          o.policy, o.dict_slack_pct, &(*out)[job.first]);
+                          o.policy, coding_options(o), &(*out)[job.first]);
       }
       {
         std::lock_guard<std::mutex> lk(mu);

@@ -93,6 +93,7 @@ class DeltaWeights:
         dict_slack_pct: int = _DICT_SLACK_PCT,
         encode_on_device: bool = True,
         encode_batch_bytes: int = 0,
+        escapes: int = 0,
     ) -> None:
         started = time.perf_counter()
         if policy not in _lib.POLICIES:
@@ -124,6 +125,7 @@ class DeltaWeights:
             dict_slack_pct=dict_slack_pct,
             encode_on_device=int(bool(encode_on_device)),
             encode_batch_bytes=encode_batch_bytes,
+            escapes=escapes,
         )
         plan = ctypes.c_void_p()
         with torch.cuda.device(self.device):
