@@ -116,6 +116,37 @@ def test_corrupt_payload_is_detected_by_the_final_state_check() -> None:
         _lib.load().ws_plan_destroy(plan)
 
 
+def escape_block(blocks):
+    return next(bk for bk in blocks if bk["flags"] & 2)
+
+
+def test_escape_lists_shrink_the_stream_and_malformed_lists_are_reported() -> None:
+    """Escape lists on the 8B-like distribution, decoded by the oracle; a lane
+    count raised by one hands that lane an entry of the next lane, which is reported."""
+    a_t, b_t = bf16_pair(1 << 20, 0.01, 12)
+    sizes = {}
+    for esc in (-1, 0):
+        work = {"w": b_t.clone()}
+        plan = host_plan({"w": a_t}, work, "xor", escapes=esc)
+        try:
+            blocks, tiles, tables, arena, stats = plan_arrays(plan)
+            sizes[esc] = int(stats.arena_bytes)
+            err, ck = ostream.apply_plan(blocks, tiles, tables, arena, 0, True, 2)
+            assert err == 0 and ck == stats.expected_checksum[1]
+            np.testing.assert_array_equal(as_bytes(work["w"]), as_bytes(a_t))
+            if esc == 0:
+                blk = escape_block(blocks)
+                side = int(blk["src"]) + ((2 * int(blk["nwords"]) + 15) & ~15)
+                counts = arena[side: side + 64].view(np.uint16)
+                lane = next(l for l in range(31) if counts[l + 1] > 0)
+                counts[lane] += 1  # lane now reads the next lane's first entry
+                err, _ = ostream.apply_plan(blocks, tiles, tables, arena, 0, False, 2)
+                assert err & 2
+        finally:
+            _lib.load().ws_plan_destroy(plan)
+    assert sizes[0] < sizes[-1] * 0.97
+
+
 def test_overlapping_targets_and_bad_options_are_rejected() -> None:
     lib = _lib.load()
     buf = torch.zeros(1000, dtype=torch.uint8)

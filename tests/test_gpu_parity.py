@@ -167,3 +167,28 @@ def test_corrupt_frame_is_reported_and_the_context_stays_usable(cuda_device) -> 
     fresh = DeltaWeights(a, gpu2, policy="xor")
     fresh.apply(reverse=True)
     assert_bytes_equal(gpu2, a)
+
+
+def test_malformed_escape_list_is_reported(cuda_device) -> None:
+    """Host-side fault injection in an escape list: a lane's count raised by one
+    makes it read the next lane's first entry, which the kernel's ownership check
+    reports as a device error; no access leaves the block or the payload."""
+    import ctypes
+
+    from oracle import stream as ostream
+    from tests.helpers import bf16_pair
+
+    x, y = bf16_pair(1 << 20, 0.01, 12)
+    gpu = {"w": y.to(cuda_device)}
+    delta = DeltaWeights({"w": x}, gpu, policy="xor")
+    view = delta.plan_view()
+    blocks = np.ctypeslib.as_array((ctypes.c_uint8 * (32 * view.nblocks)).from_address(view.blocks)).view(ostream.BLOCK_DTYPE)
+    arena = np.ctypeslib.as_array((ctypes.c_uint8 * view.arena_bytes).from_address(view.arena))
+    blk = next(bk for bk in blocks if bk["flags"] & 2)
+    side = int(blk["src"]) + ((2 * int(blk["nwords"]) + 15) & ~15)
+    counts = arena[side: side + 64].view(np.uint16)
+    lane = next(l for l in range(31) if counts[l + 1] > 0)
+    counts[lane] += 1  # lane now reads the next lane's first entry
+    with pytest.raises(RuntimeError, match="decode failed"):
+        delta.apply(reverse=True)
+    assert delta.last_apply["device_errors"] & 2
