@@ -4,8 +4,9 @@ Same Python surface as warpshift/delta.py:95-327: ``DeltaWeights(cpu_base,
 gpu_target)``, ``.apply(reverse)``, ``.validate_bindings()``, ``.bindings``,
 ``.device``, ``.stats`` and the module helpers ``_u16_residual`` and
 ``_batch_layout``. Underneath, nvCOMP and the Triton ``_restore_batch`` kernel
-are replaced by ``libwarpshift_b200.so``: a multi-threaded host rANS encoder for
-prepare and one fused sm_100a decode+apply kernel per staging batch for apply.
+are replaced by ``libwarpshift_b200.so``: a GPU encoder for prepare (statistics,
+rANS encode and packing kernels; host encoder threads as fallback) and one fused
+sm_100a decode+apply kernel per staging batch for apply.
 
 Per-packet mode choice keeps the reference rule (delta.py:176-194: raw XOR, then
 grouped/odd XOR-ANS, then U16-ANS, strictly-smaller wins). The keyword-only
@@ -78,7 +79,16 @@ class DeltaWeights:
 
     ``cpu_base`` contains A and ``gpu_target`` currently contains B. Construction
     never changes GPU weights and keeps no full CPU copy of A: only the encoded
-    stream, in one pinned host arena.
+    stream, in pinned host memory.
+
+    Keyword-only options beyond the reference: ``policy`` ("auto" = the
+    reference's mode rule, "xor", "u16"), ``threads`` (host threads; 0 = all),
+    ``batch_bytes`` (bound on one H2D staging batch), ``staging_slots``,
+    ``dict_slack_pct`` (word-dictionary coding when within this many percent of
+    the byte planes' size; negative = never), ``encode_on_device`` (prepare on
+    the GPU), ``encode_batch_bytes`` (GPU encoder batch; 0 = 512 MiB) and
+    ``escapes`` (dictionaries with escape lists: 0 when smaller, -1 never, 1
+    whenever eligible). ``save`` / ``load`` persist a package across restarts.
     """
 
     def __init__(
