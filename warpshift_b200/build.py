@@ -17,7 +17,7 @@ PACKAGE = Path(__file__).resolve().parent
 CSRC = PACKAGE / "csrc"
 LIBRARY = PACKAGE / "libwarpshift_b200.so"
 SOURCES = ["ws_apply.cu", "ws_gpu_encoder.cu", "ws_hash.cu", "ws_encoder.cpp", "ws_plan.cpp", "ws_persist.cpp"]
-HEADERS = ["ws_format.h", "ws_encoder.h", "ws_kernels.h", "ws_gpu_encoder.h", "ws_plan_internal.h", "../../include/warpshift_b200.h"]
+HEADERS = ["ws_format.h", "ws_encoder.h", "ws_kernels.h", "ws_gpu_encoder.h", "ws_plan_internal.h", "ws_guard.h", "../../include/warpshift_b200.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -22,6 +22,7 @@
 #include <stdint.h>
 
 #include "ws_format.h"
+#include "ws_guard.h"
 #include "ws_kernels.h"
 
 namespace ws {
@@ -812,7 +813,7 @@ int noalloc_scratch(int device, ws_device_result** out) {
 }  // namespace
 }  // namespace ws
 
-extern "C" WS_API int ws_apply_device_noalloc(const void* tiles, uint32_t ntiles, const void* blocks,
+static int ws_apply_device_noalloc_impl(const void* tiles, uint32_t ntiles, const void* blocks,
                                               const uint32_t* tables, const void* payload, int reverse, int device,
                                               void* stream, ws_apply_result* out) {
   using namespace ws;
@@ -881,6 +882,12 @@ extern "C" WS_API int ws_apply_device_noalloc(const void* tiles, uint32_t ntiles
   return done(WS_OK);
 }
 
+extern "C" WS_API int ws_apply_device_noalloc(const void* tiles, uint32_t ntiles, const void* blocks,
+                                              const uint32_t* tables, const void* payload, int reverse, int device,
+                                              void* stream, ws_apply_result* out) {
+  return ws::guarded([&] { return ws_apply_device_noalloc_impl(tiles, ntiles, blocks, tables, payload, reverse, device, stream, out); });
+}
+
 // ---------------------------------------------------------------------------
 // Failure-path self-test (ws_selftest_wait_timeout in include/warpshift_b200.h).
 // One warp waits, with the decode kernel's bounded wait, on a staging barrier
@@ -904,7 +911,7 @@ __global__ void ws_wait_selftest_kernel(uint32_t limit, ws_device_result* res) {
 }  // namespace
 }  // namespace ws
 
-extern "C" WS_API int ws_selftest_wait_timeout(uint32_t polls, int device, void* stream, uint32_t* device_errors) {
+static int ws_selftest_wait_timeout_impl(uint32_t polls, int device, void* stream, uint32_t* device_errors) {
   using namespace ws;
   if (!device_errors || polls == 0 || polls > kWaitLimit) {
     set_last_error("ws_selftest_wait_timeout: need 1 <= polls <= 2^20 and a result pointer");
@@ -933,4 +940,8 @@ extern "C" WS_API int ws_selftest_wait_timeout(uint32_t polls, int device, void*
   }
   *device_errors = h.errors;
   return WS_OK;
+}
+
+extern "C" WS_API int ws_selftest_wait_timeout(uint32_t polls, int device, void* stream, uint32_t* device_errors) {
+  return ws::guarded([&] { return ws_selftest_wait_timeout_impl(polls, device, stream, device_errors); });
 }

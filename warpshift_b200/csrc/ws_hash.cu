@@ -18,6 +18,7 @@
 
 #include "../../include/warpshift_b200.h"
 #include "ws_format.h"
+#include "ws_guard.h"
 
 namespace ws {
 void set_last_error(const char* msg);
@@ -104,7 +105,7 @@ int fail(int code, const std::string& msg) {
 
 }  // namespace
 
-extern "C" int ws_tensor_hashes(const void* const* ptrs, const uint64_t* nbytes, uint64_t n, int device, void* stream,
+static int ws_tensor_hashes_impl(const void* const* ptrs, const uint64_t* nbytes, uint64_t n, int device, void* stream,
                                 uint64_t* out) {
   if (n && (!ptrs || !nbytes || !out)) return fail(WS_ERR_INVALID, "null argument");
   std::vector<HashTensor> list;
@@ -153,4 +154,9 @@ extern "C" int ws_tensor_hashes(const void* const* ptrs, const uint64_t* nbytes,
   for (size_t k = 0; k < list.size(); ++k)
     out[owner[k]] = ws_mix64((uint64_t)acc[k] + (uint64_t)(nbytes[owner[k]] + 1) * WS_TH_KLEN);
   return WS_OK;
+}
+
+extern "C" int ws_tensor_hashes(const void* const* ptrs, const uint64_t* nbytes, uint64_t n, int device, void* stream,
+                                uint64_t* out) {
+  return ws::guarded([&] { return ws_tensor_hashes_impl(ptrs, nbytes, n, device, stream, out); });
 }

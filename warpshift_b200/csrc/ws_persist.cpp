@@ -32,6 +32,7 @@
 
 #include "../../include/warpshift_b200.h"
 #include "ws_format.h"
+#include "ws_guard.h"
 #include "ws_gpu_encoder.h"
 #include "ws_plan_internal.h"
 
@@ -169,7 +170,7 @@ std::string check_descriptors(const ws_plan* p) {
 
 extern "C" {
 
-int ws_plan_save(const ws_plan* p, const char* path) {
+static int ws_plan_save_impl(const ws_plan* p, const char* path) {
   if (!p || !path) return fail(WS_ERR_INVALID, "null argument");
   if (p->block_tensor.size() != p->blocks.size()) return fail(WS_ERR_STATE, "plan has no tensor map");
   std::vector<uint8_t> meta;
@@ -214,7 +215,11 @@ int ws_plan_save(const ws_plan* p, const char* path) {
   return WS_OK;
 }
 
-int ws_plan_load(const char* path, const ws_tensor_desc* tensors, uint64_t ntensors, const ws_build_options* opts,
+int ws_plan_save(const ws_plan* p, const char* path) {
+  return ws::guarded([&] { return ws_plan_save_impl(p, path); });
+}
+
+static int ws_plan_load_impl(const char* path, const ws_tensor_desc* tensors, uint64_t ntensors, const ws_build_options* opts,
                  ws_plan** out) {
   if (!path || !opts || !out || (ntensors && !tensors)) return fail(WS_ERR_INVALID, "null argument");
   *out = nullptr;
@@ -324,6 +329,11 @@ int ws_plan_load(const char* path, const ws_tensor_desc* tensors, uint64_t ntens
   p->stats.encode_seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - started).count();
   *out = p;
   return WS_OK;
+}
+
+int ws_plan_load(const char* path, const ws_tensor_desc* tensors, uint64_t ntensors, const ws_build_options* opts,
+                 ws_plan** out) {
+  return ws::guarded([&] { return ws_plan_load_impl(path, tensors, ntensors, opts, out); });
 }
 
 }  // extern "C"

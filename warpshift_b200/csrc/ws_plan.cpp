@@ -25,6 +25,7 @@
 #include "../../include/warpshift_b200.h"
 #include "ws_encoder.h"
 #include "ws_format.h"
+#include "ws_guard.h"
 #include "ws_gpu_encoder.h"
 #include "ws_kernels.h"
 #include "ws_plan_internal.h"
@@ -36,7 +37,10 @@ using ws::Batch;
 thread_local std::string g_last_error;
 
 int fail(int code, const std::string& msg) {
-  g_last_error = msg;
+  try {
+    g_last_error = msg;
+  } catch (...) {
+  }
   return code;
 }
 
@@ -83,7 +87,12 @@ void parallel_for(uint64_t n, int threads, F fn) {
 
 namespace ws {
 // Lets entry points defined in other translation units record ws_last_error().
-void set_last_error(const char* msg) { g_last_error = msg; }
+void set_last_error(const char* msg) {
+  try {
+    g_last_error = msg;
+  } catch (...) {  // out of memory for the message itself: keep the previous one
+  }
+}
 }  // namespace ws
 
 
@@ -430,7 +439,7 @@ int ws_u16_residual(const uint8_t* base, const uint8_t* target, uint64_t nbytes,
   return WS_OK;
 }
 
-int ws_plan_build(const ws_tensor_desc* tensors, uint64_t ntensors, const ws_build_options* opts, void* stream,
+static int ws_plan_build_impl(const ws_tensor_desc* tensors, uint64_t ntensors, const ws_build_options* opts, void* stream,
                   ws_plan** out) {
   if (!out || !opts || (ntensors && !tensors)) return fail(WS_ERR_INVALID, "null argument");
   *out = nullptr;
@@ -503,7 +512,12 @@ int ws_plan_build(const ws_tensor_desc* tensors, uint64_t ntensors, const ws_bui
   return WS_OK;
 }
 
-int ws_plan_upload(ws_plan* p, void* stream) {
+int ws_plan_build(const ws_tensor_desc* tensors, uint64_t ntensors, const ws_build_options* opts, void* stream,
+                  ws_plan** out) {
+  return ws::guarded([&] { return ws_plan_build_impl(tensors, ntensors, opts, stream, out); });
+}
+
+static int ws_plan_upload_impl(ws_plan* p, void* stream) {
   if (!p) return fail(WS_ERR_INVALID, "null plan");
   if (p->device < 0) return fail(WS_ERR_STATE, "plan was built for host targets; nothing to upload");
   if (p->uploaded) return WS_OK;
@@ -554,7 +568,11 @@ int ws_plan_upload(ws_plan* p, void* stream) {
   return WS_OK;
 }
 
-int ws_plan_set_resident(ws_plan* p, int resident, void* stream) {
+int ws_plan_upload(ws_plan* p, void* stream) {
+  return ws::guarded([&] { return ws_plan_upload_impl(p, stream); });
+}
+
+static int ws_plan_set_resident_impl(ws_plan* p, int resident, void* stream) {
   if (!p) return fail(WS_ERR_INVALID, "null plan");
   if (!p->uploaded) return fail(WS_ERR_STATE, "upload the plan first");
   int prev = -1;
@@ -582,7 +600,11 @@ int ws_plan_set_resident(ws_plan* p, int resident, void* stream) {
   return WS_OK;
 }
 
-int ws_apply_async(ws_plan* p, int reverse, void* compute_stream, void* copy_stream) {
+int ws_plan_set_resident(ws_plan* p, int resident, void* stream) {
+  return ws::guarded([&] { return ws_plan_set_resident_impl(p, resident, stream); });
+}
+
+static int ws_apply_async_impl(ws_plan* p, int reverse, void* compute_stream, void* copy_stream) {
   if (!p) return fail(WS_ERR_INVALID, "null plan");
   if (!p->uploaded) return fail(WS_ERR_STATE, "upload the plan before applying");
   reverse = reverse ? 1 : 0;
@@ -636,7 +658,11 @@ int ws_apply_async(ws_plan* p, int reverse, void* compute_stream, void* copy_str
   return WS_OK;
 }
 
-int ws_apply_finish(ws_plan* p, void* compute_stream, ws_apply_result* out) {
+int ws_apply_async(ws_plan* p, int reverse, void* compute_stream, void* copy_stream) {
+  return ws::guarded([&] { return ws_apply_async_impl(p, reverse, compute_stream, copy_stream); });
+}
+
+static int ws_apply_finish_impl(ws_plan* p, void* compute_stream, ws_apply_result* out) {
   if (!p) return fail(WS_ERR_INVALID, "null plan");
   if (p->pending_reverse < 0) return fail(WS_ERR_STATE, "no apply in flight");
   int prev = -1;
@@ -672,6 +698,10 @@ int ws_apply_finish(ws_plan* p, void* compute_stream, ws_apply_result* out) {
   return WS_OK;
 }
 
+int ws_apply_finish(ws_plan* p, void* compute_stream, ws_apply_result* out) {
+  return ws::guarded([&] { return ws_apply_finish_impl(p, compute_stream, out); });
+}
+
 int ws_apply(ws_plan* p, int reverse, void* compute_stream, void* copy_stream, ws_apply_result* out) {
   int rc = ws_apply_async(p, reverse, compute_stream, copy_stream);
   if (rc != WS_OK) return rc;
@@ -684,7 +714,7 @@ int ws_plan_get_stats(const ws_plan* p, ws_plan_stats* out) {
   return WS_OK;
 }
 
-int ws_plan_get_view(const ws_plan* p, ws_plan_view* out) {
+static int ws_plan_get_view_impl(const ws_plan* p, ws_plan_view* out) {
   if (!p || !out) return fail(WS_ERR_INVALID, "null argument");
   const uint8_t* arena = p->chunks.empty() ? nullptr : p->chunks[0].ptr;
   if (p->chunks.size() > 1) {  // one contiguous host copy, made once
@@ -707,6 +737,10 @@ int ws_plan_get_view(const ws_plan* p, ws_plan_view* out) {
   out->arena = arena;
   out->arena_bytes = p->arena_bytes;
   return WS_OK;
+}
+
+int ws_plan_get_view(const ws_plan* p, ws_plan_view* out) {
+  return ws::guarded([&] { return ws_plan_get_view_impl(p, out); });
 }
 
 void ws_plan_destroy(ws_plan* p) {
