@@ -54,6 +54,75 @@ def edge_pair(seed: int = 0, scale: float = 0.01, big: bool = True) -> tuple[dic
     return a, b
 
 
+def _lane_positions(lane: int, count: int) -> np.ndarray:
+    """Word indexes of a 64 KiB block that decode lane ``lane`` owns: words
+    8*lane .. 8*lane+7 of every 256-word (512-byte) group, in stream order."""
+    groups = np.arange((count + 7) // 8)[:, None] * 256
+    return (groups + 8 * lane + np.arange(8)[None, :]).reshape(-1)[:count]
+
+
+def adversarial_pair(seed: int = 0) -> tuple[dict[str, torch.Tensor], dict[str, torch.Tensor]]:
+    """CPU A/B dicts whose residuals sit on the coding boundaries.
+
+    Every pattern is built twice: as an XOR residual (B = A ^ r) and as a U16
+    residual (B = A + d mod 2^16), so that both transforms meet it exactly.
+    Patterns: a single changed word among three 64 KiB blocks, two distinct
+    words, exactly 255 and 256 distinct words (the dictionary limit), extreme
+    skew (one word 99.9 %), rare words that fill one decode lane's escape list
+    to its limit of 64 and past it, one residual word everywhere (a single
+    symbol of probability 1 per table), and the largest U16 steps (d = 0x8000,
+    0x7FFF, -1). Plus a packet of exactly 16 MiB and an odd-sized multi-block
+    uint8 tensor with a three-word alphabet and a changed tail byte.
+    """
+    rng = np.random.default_rng(seed)
+    a: dict[str, torch.Tensor] = {}
+    b: dict[str, torch.Tensor] = {}
+
+    def base_words(n: int) -> np.ndarray:
+        x, _ = bf16_pair(n, 0.0, int(rng.integers(1 << 30)))
+        return x.view(torch.int16).numpy().view(np.uint16).copy()
+
+    def put_words(name: str, r: np.ndarray) -> None:
+        w = base_words(r.size)
+        for kind, t in (("x", w ^ r), ("u", (w.astype(np.uint32) + r) & 0xFFFF)):
+            a[f"parameter:{name}_{kind}"] = torch.from_numpy(w.view(np.int16).copy()).view(torch.bfloat16)
+            b[f"parameter:{name}_{kind}"] = torch.from_numpy(t.astype(np.uint16).view(np.int16)).view(torch.bfloat16)
+
+    def alphabet(size: int, n: int) -> np.ndarray:
+        values = rng.permutation(np.arange(1, 65536, dtype=np.uint32))[: size - 1]
+        values = np.concatenate([[0], values]).astype(np.uint32)
+        r = values[rng.integers(0, size, n)]
+        r[:size] = values  # every value at least once
+        return r[rng.permutation(n)]
+
+    r = np.zeros(3 * 32768, np.uint32)
+    r[40000] = 0x0040
+    put_words("one_word", r)
+    put_words("two_words", rng.integers(0, 2, 2 * 32768).astype(np.uint32))
+    put_words("distinct_255", alphabet(255, 2 * 32768 + 100))
+    put_words("distinct_256", alphabet(256, 2 * 32768 + 100))
+    r = np.where(rng.random(2 * 32768) < 0.999, 0, rng.integers(1, 4, 2 * 32768)).astype(np.uint32)
+    put_words("skew", r)
+    for escapes in (64, 126):
+        # 192 frequent words (the largest dictionary kept beside escapes) and
+        # escapes / 2 rare words, each twice, all in lane 5 of the first block.
+        frequent = rng.permutation(np.arange(1, 65536, dtype=np.uint32))[:192]
+        r = frequent[rng.integers(0, 192, 2 * 32768)]
+        pool = np.setdiff1d(np.arange(1, 65536, dtype=np.uint32), frequent)
+        r[_lane_positions(5, escapes)] = np.repeat(rng.choice(pool, escapes // 2, replace=False), 2)
+        put_words(f"lane5_escapes_{escapes}", r)
+    for word in (0x0101, 0x8000, 0xFFFF):  # one residual word everywhere: single-symbol tables
+        put_words(f"constant_{word:04x}", np.full(2 * 32768 + 50, word, np.uint32))
+    steps = np.array([0, 0x8000, 0x7FFF, 0xFFFF, 1], np.uint32)
+    put_words("u16_extremes", steps[rng.integers(0, 5, 32768 + 4096)])
+    put_words("packet_16mib", alphabet(40, (16 << 20) // 2))
+    u = rng.integers(0, 256, 3 * 65536 + 3, dtype=np.uint8)
+    v = u ^ np.array([0, 1, 2], np.uint8)[rng.integers(0, 3, u.size)]
+    v[-1] = u[-1] ^ 0x80
+    a["buffer:u8_odd_blocks"], b["buffer:u8_odd_blocks"] = torch.from_numpy(u), torch.from_numpy(v)
+    return a, b
+
+
 def host_plan(a: dict[str, torch.Tensor], b: dict[str, torch.Tensor], policy: str, threads: int = 4, dict_slack_pct: int = 6,
               escapes: int = 0):
     """Build a plan on host targets (no GPU); b's tensors are the destinations."""

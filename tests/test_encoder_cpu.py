@@ -17,7 +17,7 @@ import torch
 
 from oracle import semantics as sem
 from oracle import stream as ostream
-from tests.helpers import as_bytes, bf16_pair, edge_pair, host_plan, plan_arrays
+from tests.helpers import adversarial_pair, as_bytes, bf16_pair, edge_pair, host_plan, plan_arrays
 from warpshift_b200 import _lib
 
 KIND_RAW, KIND_XOR, KIND_U16, KIND_DICT_XOR, KIND_DICT_U16 = 0, 1, 2, 3, 4
@@ -47,6 +47,67 @@ def test_host_plan_round_trips_through_the_oracle_decoder(policy: str, coding: s
             assert checksum == stats.expected_checksum[1 if reverse else 0]
             for name in b:
                 np.testing.assert_array_equal(as_bytes(work[name]), as_bytes(teacher[name]), err_msg=name)
+    finally:
+        _lib.load().ws_plan_destroy(plan)
+
+
+@pytest.fixture(scope="module")
+def adversarial():
+    return adversarial_pair(seed=5)
+
+
+def blocks_by_tensor(blocks, work) -> dict[str, list]:
+    """The plan's blocks grouped by destination tensor, in stream order."""
+    spans = [(t.data_ptr(), t.data_ptr() + t.numel() * t.element_size(), n.split(":")[1]) for n, t in work.items()]
+    out: dict[str, list] = {}
+    for bk in blocks:
+        dst = int(bk["dst"])
+        out.setdefault(next(n for lo, hi, n in spans if lo <= dst < hi), []).append(bk)
+    return out
+
+
+@pytest.mark.parametrize("coding", list(CODINGS))
+@pytest.mark.parametrize("policy", ["auto", "xor", "u16"])
+def test_boundary_residuals_round_trip_through_the_oracle_decoder(adversarial, policy: str, coding: str) -> None:
+    a, b = adversarial
+    work = clone(b)
+    plan = host_plan(a, work, policy, dict_slack_pct=CODINGS[coding][0], escapes=CODINGS[coding][1])
+    try:
+        blocks, tiles, tables, arena, stats = plan_arrays(plan)
+        for reverse, teacher in ((True, a), (False, b), (True, a)):
+            err, checksum = ostream.apply_plan(blocks, tiles, tables, arena, 0, reverse, 4)
+            assert err == 0
+            assert checksum == stats.expected_checksum[1 if reverse else 0]
+            for name in b:
+                np.testing.assert_array_equal(as_bytes(work[name]), as_bytes(teacher[name]), err_msg=name)
+    finally:
+        _lib.load().ws_plan_destroy(plan)
+
+
+@pytest.mark.parametrize("policy, suffix, dict_kind", [("xor", "x", KIND_DICT_XOR), ("u16", "u", KIND_DICT_U16)])
+def test_dictionary_and_escape_limits_are_exact(adversarial, policy: str, suffix: str, dict_kind: int) -> None:
+    """255 distinct words fit a dictionary, 256 do not; a lane holds at most 64
+    escapes, and a block that needs more is carried raw."""
+    a, b = adversarial
+    work = clone(b)
+    plan = host_plan(a, work, policy, dict_slack_pct=100, escapes=1)
+    try:
+        blocks, tiles, tables, arena, stats = plan_arrays(plan)
+        by = blocks_by_tensor(blocks, work)
+        kinds = {n: {int(bk["kind"]) for bk in bks} for n, bks in by.items()}
+        assert dict_kind in kinds[f"distinct_255_{suffix}"]
+        assert dict_kind not in kinds[f"distinct_256_{suffix}"]
+        first, second = by[f"lane5_escapes_64_{suffix}"]
+        assert first["kind"] == dict_kind and first["flags"] & 2
+        side = int(first["src"]) + ((2 * int(first["nwords"]) + 15) & ~15)
+        counts = arena[side : side + 64].view(np.uint16)
+        assert counts[5] == 64 and counts.sum() == 64
+        first, second = by[f"lane5_escapes_126_{suffix}"]
+        assert first["kind"] == KIND_RAW and second["kind"] == dict_kind and not second["flags"] & 2
+        err, _ = ostream.apply_plan(blocks, tiles, tables, arena, 0, True, 4)
+        assert err == 0
+        for name in a:
+            np.testing.assert_array_equal(as_bytes(work[name]), as_bytes(a[name]), err_msg=name)
     finally:
         _lib.load().ws_plan_destroy(plan)
 

@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 import torch
 
-from tests.helpers import bf16_pair, edge_pair, plan_arrays
+from tests.helpers import adversarial_pair, bf16_pair, edge_pair, plan_arrays
 from warpshift_b200 import _lib
 
 pytestmark = pytest.mark.gpu
@@ -54,6 +54,29 @@ def assert_same_plan(p_gpu, p_host) -> None:
 @pytest.mark.parametrize("policy", ["auto", "xor", "u16"])
 def test_gpu_encoder_matches_host_encoder(cuda_device, policy: str, slack: int, escapes: int) -> None:
     a, b = edge_pair(seed=13)
+    b_dev = {k: v.to(cuda_device) for k, v in b.items()}
+    lib = _lib.load()
+    p_gpu = build(a, b_dev, policy, slack, True, escapes=escapes)
+    p_host = build(a, b_dev, policy, slack, False, escapes=escapes)
+    try:
+        assert_same_plan(p_gpu, p_host)
+    finally:
+        lib.ws_plan_destroy(p_gpu)
+        lib.ws_plan_destroy(p_host)
+
+
+@pytest.fixture(scope="module")
+def adversarial():
+    return adversarial_pair(seed=5)
+
+
+@pytest.mark.parametrize("slack, escapes", [(-1, -1), (6, 0), (100, 1)])
+@pytest.mark.parametrize("policy", ["auto", "xor", "u16"])
+def test_gpu_encoder_matches_host_encoder_on_coding_limits(cuda_device, adversarial, policy: str, slack: int,
+                                                          escapes: int) -> None:
+    """255/256 distinct words (the device word table's limit), a lane's escape
+    list at 64 entries and past it, extreme skew, an exact 16 MiB packet."""
+    a, b = adversarial
     b_dev = {k: v.to(cuda_device) for k, v in b.items()}
     lib = _lib.load()
     p_gpu = build(a, b_dev, policy, slack, True, escapes=escapes)

@@ -13,7 +13,7 @@ import pytest
 import torch
 
 from oracle import semantics as sem
-from tests.helpers import as_bytes, edge_pair
+from tests.helpers import adversarial_pair, as_bytes, edge_pair
 from warpshift_b200 import synth
 from warpshift_b200.delta import DeltaWeights
 
@@ -48,6 +48,26 @@ def test_edge_cases_round_trip_bit_exact(cuda_device, policy: str, coding: str) 
         delta.apply(reverse=reverse)
         assert_bytes_equal(gpu, expected)
         assert delta.last_apply["ok"] and delta.last_apply["checksum"] == delta.last_apply["expected"]
+
+
+@pytest.fixture(scope="module")
+def adversarial():
+    return adversarial_pair(seed=5)
+
+
+@pytest.mark.parametrize("coding", list(CODINGS))
+@pytest.mark.parametrize("policy", ["auto", "xor", "u16"])
+def test_boundary_residuals_round_trip_bit_exact(cuda_device, adversarial, policy: str, coding: str) -> None:
+    """Residuals on the coding limits (255/256 distinct words, 64 escapes in one
+    lane and more, one changed word, extreme skew, largest U16 steps, an exact
+    16 MiB packet), encoded on the GPU and applied by the fused kernel."""
+    a, b = adversarial
+    gpu = to_device(b, cuda_device)
+    delta = DeltaWeights(a, gpu, policy=policy, dict_slack_pct=CODINGS[coding][0], escapes=CODINGS[coding][1])
+    for reverse, expected in ((True, a), (False, b), (True, a)):
+        delta.apply(reverse=reverse)
+        assert_bytes_equal(gpu, expected)
+        assert delta.last_apply["ok"]
 
 
 @pytest.mark.parametrize("coding", list(CODINGS))
