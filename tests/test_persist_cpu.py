@@ -135,6 +135,74 @@ def test_corrupt_truncated_and_foreign_files_are_rejected(saved, tmp_path) -> No
     assert not (tmp_path / "delta.wsd.tmp").exists()
 
 
+def rehashed(raw: bytes, edit) -> bytes:
+    """The saved file with its block/tile descriptors changed by ``edit`` and the
+    metadata hash recomputed, so that only the descriptor checks can reject it.
+    Header: magic, u32 version/header/stats/block-desc sizes, then u64 counts,
+    arena offset and size, metadata hash (ws_persist.cpp)."""
+    from oracle.hashes import mix64_int
+
+    head = np.frombuffer(raw[:80], dtype=np.uint8)
+    stats_bytes = int(head[16:20].view("<u4")[0])
+    ntensors, nblocks, ntiles, _, arena_offset, _, _ = (int(x) for x in head[24:80].view("<u8"))
+    meta = bytearray(raw[80:arena_offset])
+    at = stats_bytes + 16 * ntensors
+    blocks = np.frombuffer(meta, dtype=ostream.BLOCK_DTYPE, count=nblocks, offset=at).copy()
+    tiles = np.frombuffer(meta, dtype=ostream.TILE_DTYPE, count=ntiles, offset=at + 36 * nblocks).copy()
+    edit(blocks, tiles)
+    meta[at : at + 32 * nblocks] = blocks.tobytes()
+    meta[at + 36 * nblocks : at + 36 * nblocks + 16 * ntiles] = tiles.tobytes()
+    h = 0x6A09E667F3BCC908 ^ len(meta)
+    words = np.frombuffer(bytes(meta), dtype="<u8")
+    for i, w in enumerate(words.tolist()):
+        h = mix64_int(h ^ ((w + (i + 1) * 0x9E3779B97F4A7C15) & ((1 << 64) - 1)))
+    out = bytearray(raw)
+    out[72:80] = np.array([h], dtype="<u8").tobytes()
+    out[80:arena_offset] = meta
+    return bytes(out)
+
+
+def test_descriptors_that_could_reach_outside_the_buffers_are_rejected(saved, tmp_path) -> None:
+    """Metadata with a valid hash but descriptors that would make a kernel write
+    outside a tensor, stage a payload with a size the bulk copies cannot take,
+    or look up a missing table is rejected before any arena is read."""
+    a, b, work, plan, path = saved
+    raw = path.read_bytes()
+    bad = tmp_path / "bad.wsd"
+    bad.write_bytes(rehashed(raw, lambda bl, ti: None))
+    lib = _lib.load()
+    lib.ws_plan_destroy(load(bad, clone(b)))  # the rewriting itself keeps the file valid
+
+    def first_coded(bl):
+        return int(np.flatnonzero(bl["kind"] != 0)[0])
+
+    def outside(bl, ti):
+        bl["dst"][0] += 1 << 40
+
+    def shift16(bl, ti):  # two payloads of lengths -8 / +8: still contiguous, no longer 16-byte multiples
+        k = first_coded(bl)
+        bl["clen"][k] -= 8
+        bl["src"][k + 1] -= 8
+        bl["clen"][k + 1] += 8
+
+    def kind(bl, ti):
+        bl["kind"][0] = 9
+
+    def table(bl, ti):
+        ti["table"][int(np.flatnonzero(ti["table"] != 0xFFFFFFFF)[0])] = 1 << 20
+
+    def stream_length(bl, ti):
+        k = first_coded(bl)
+        bl["nwords"][k] = bl["clen"][k]  # 2 * nwords bytes no longer fit the payload
+
+    cases = {outside: "writes outside its tensor", shift16: "not a multiple of 16", kind: "unknown kind",
+             table: "bad table", stream_length: "bad stream length"}
+    for edit, message in cases.items():
+        bad.write_bytes(rehashed(raw, edit))
+        with pytest.raises(ValueError, match=message):
+            load(bad, clone(b))
+
+
 def test_empty_model_round_trips(tmp_path) -> None:
     a = {"w": torch.zeros(1000, dtype=torch.bfloat16)}
     b = clone(a)

@@ -139,6 +139,9 @@ std::string check_descriptors(const ws_plan* p) {
     if (d.nbytes == 0 || d.nbytes > WS_BLOCK_BYTES) return "block " + std::to_string(k) + " has a bad size";
     if (d.dst > p->tensor_bytes[t] || d.nbytes > p->tensor_bytes[t] - d.dst)
       return "block " + std::to_string(k) + " writes outside its tensor";
+    // Payloads are staged with bulk copies, whose sizes and addresses must be
+    // multiples of 16 bytes; contiguous 16-byte lengths keep every source aligned.
+    if (d.clen % 16u != 0) return "block " + std::to_string(k) + " has a payload length that is not a multiple of 16";
     if (d.src != next_src) return "block payloads are not contiguous in block order";
     next_src += d.clen;
     if (d.kind == WS_KIND_RAW) {
