@@ -149,7 +149,8 @@ WS_API int ws_plan_build(const ws_tensor_desc* tensors, uint64_t ntensors, const
 WS_API int ws_plan_upload(ws_plan* plan, void* stream);
 
 /* resident=1 keeps a device copy of the whole arena so applies skip the H2D
- * staging (kernel-only timing); resident=0 frees it. */
+ * staging (kernel-only timing); resident=0 frees it once the applies in flight
+ * have completed. */
 WS_API int ws_plan_set_resident(ws_plan* plan, int resident, void* stream);
 
 /* Replaces DeltaWeights.apply (delta.py:294-327): A->B when reverse == 0, B->A when 1.
@@ -161,7 +162,9 @@ WS_API int ws_plan_set_resident(ws_plan* plan, int resident, void* stream);
 WS_API int ws_apply(ws_plan* plan, int reverse, void* compute_stream, void* copy_stream, ws_apply_result* out);
 
 /* Asynchronous halves of ws_apply: enqueue only (no host synchronisation), then
- * wait for compute_stream and evaluate the result. */
+ * wait for compute_stream and evaluate the result. ws_apply_async may be called
+ * again on the same compute_stream before ws_apply_finish: the applies run in
+ * stream order and ws_apply_finish reports the last one. */
 WS_API int ws_apply_async(ws_plan* plan, int reverse, void* compute_stream, void* copy_stream);
 WS_API int ws_apply_finish(ws_plan* plan, void* compute_stream, ws_apply_result* out);
 
@@ -224,7 +227,8 @@ WS_API int ws_tensor_hashes(const void* const* ptrs, const uint64_t* nbytes, uin
  * completes. */
 WS_API int ws_selftest_wait_timeout(uint32_t polls, int device, void* stream, uint32_t* device_errors);
 
-/* Frees host and device resources (delta.py relies on GC for the same). */
+/* Frees host and device resources (delta.py relies on GC for the same), after
+ * waiting for an apply still in flight. */
 WS_API void ws_plan_destroy(ws_plan* plan);
 
 #ifdef __cplusplus

@@ -124,6 +124,32 @@ def test_config0_qwen2_shape_matches_reference_semantics(cuda_device) -> None:
     assert_bytes_equal(gpu, t2)
 
 
+def test_async_applies_run_in_stream_order_and_teardown_waits(cuda_device) -> None:
+    """Back-to-back apply_async calls (the kernel-only bench loop) run in stream
+    order and finish reports the last; freeing the resident copy or the whole
+    plan with an apply in flight waits for it first."""
+    a, b = edge_pair(seed=6, big=False)
+    gpu = to_device(b, cuda_device)
+    delta = DeltaWeights(a, gpu, policy="auto")
+    for resident in (True, False):
+        delta.set_resident(resident)
+        for k in range(3):  # B->A, A->B, B->A
+            delta.apply_async(reverse=k % 2 == 0)
+        assert delta.finish()["ok"]
+        assert_bytes_equal(gpu, a)
+        delta.apply(reverse=False)
+        assert_bytes_equal(gpu, b)
+    delta.set_resident(True)
+    delta.apply_async(reverse=True)
+    delta.set_resident(False)
+    assert delta.finish()["ok"]
+    assert_bytes_equal(gpu, a)
+    delta.apply_async(reverse=False)
+    delta.close()
+    torch.cuda.synchronize(cuda_device)
+    assert_bytes_equal(gpu, b)
+
+
 def test_checksum_rejects_wrong_resident_model(cuda_device) -> None:
     a, b = edge_pair(seed=3, big=False)
     gpu = to_device(b, cuda_device)

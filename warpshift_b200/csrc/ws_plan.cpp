@@ -103,6 +103,8 @@ void release_device(ws_plan* p) {
   int prev = -1;
   cudaGetDevice(&prev);
   cudaSetDevice(p->device);
+  // An apply still in flight reads these buffers and writes h_result.
+  if (p->done_event) cudaEventSynchronize(p->done_event);
   cudaFree(p->d_blocks);
   cudaFree(p->d_tiles);
   cudaFree(p->d_tables);
@@ -114,6 +116,7 @@ void release_device(ws_plan* p) {
   for (auto e : p->compute_done) cudaEventDestroy(e);
   if (p->start_event) cudaEventDestroy(p->start_event);
   if (p->aux_done) cudaEventDestroy(p->aux_done);
+  if (p->done_event) cudaEventDestroy(p->done_event);
   if (p->own_copy_stream) cudaStreamDestroy(p->own_copy_stream);
   if (p->aux_stream) cudaStreamDestroy(p->aux_stream);
   p->d_blocks = nullptr;
@@ -127,6 +130,7 @@ void release_device(ws_plan* p) {
   p->compute_done.clear();
   p->start_event = nullptr;
   p->aux_done = nullptr;
+  p->done_event = nullptr;
   p->own_copy_stream = nullptr;
   p->aux_stream = nullptr;
   p->uploaded = false;
@@ -555,6 +559,7 @@ static int ws_plan_upload_impl(ws_plan* p, void* stream) {
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p->own_copy_stream, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->aux_done, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p->aux_stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->done_event, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) {
     std::string msg = std::string("upload: ") + cudaGetErrorString(e);
@@ -592,6 +597,7 @@ static int ws_plan_set_resident_impl(ws_plan* p, int resident, void* stream) {
     }
     p->stats.scratch_bytes += p->arena_bytes;
   } else if (!resident && p->d_resident) {
+    WS_CUDA_TRY(cudaEventSynchronize(p->done_event));  // applies in flight read the resident copy
     cudaFree(p->d_resident);
     p->d_resident = nullptr;
     p->stats.scratch_bytes -= p->arena_bytes;
@@ -651,6 +657,7 @@ static int ws_apply_async_impl(ws_plan* p, int reverse, void* compute_stream, vo
     WS_CUDA_TRY(cudaStreamWaitEvent(comp, p->aux_done, 0));
   }
   WS_CUDA_TRY(cudaMemcpyAsync(p->h_result, p->d_result, sizeof(ws_device_result), cudaMemcpyDeviceToHost, comp));
+  WS_CUDA_TRY(cudaEventRecord(p->done_event, comp));
   p->pending_reverse = reverse;
   p->pending_h2d = h2d;
   p->pending_launches = launches;

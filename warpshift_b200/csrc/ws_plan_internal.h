@@ -51,6 +51,7 @@ struct ws_plan {
   cudaEvent_t aux_done = nullptr;        // end of the second compute stream's work
   cudaStream_t own_copy_stream = nullptr;
   cudaStream_t aux_stream = nullptr;     // runs every other staging batch's kernel
+  cudaEvent_t done_event = nullptr;      // recorded after each apply's last operation
 
   int pending_reverse = -1;
   uint64_t pending_h2d = 0;
