@@ -123,6 +123,57 @@ def adversarial_pair(seed: int = 0) -> tuple[dict[str, torch.Tensor], dict[str, 
     return a, b
 
 
+def random_pair(size_class: tuple[int, int], kind: str, param: float, transform: str, odd: bool,
+                seed: int) -> tuple[dict[str, torch.Tensor], dict[str, torch.Tensor]]:
+    """A seeded random A/B pair for property tests: one bf16 tensor whose word
+    count is drawn from ``size_class`` and whose residual is bf16 relative noise of
+    strength ``param`` ("noise"), a skewed alphabet of 1 + 400 * param words
+    ("alphabet") or a fraction param / 10 of changed words ("sparse"), applied as
+    XOR or as a wrapping U16 add (``transform``); with ``odd``, also the same
+    bytes as a uint8 tensor of odd length."""
+    rng = np.random.default_rng(seed)
+    n = int(rng.integers(size_class[0], size_class[1] + 1))
+    if kind == "noise":
+        a_t, b_t = bf16_pair(n, param, seed)
+    else:
+        if kind == "alphabet":
+            size = 1 + int(param * 400)
+            values = rng.integers(0, 65536, size).astype(np.uint32)
+            r = values[rng.choice(size, n, p=rng.dirichlet(np.full(size, 0.3)))]
+        else:
+            r = np.zeros(n, np.uint32)
+            hit = rng.random(n) < param / 10
+            r[hit] = rng.integers(1, 65536, int(hit.sum()))
+        a_t, _ = bf16_pair(n, 0.0, seed)
+        w = a_t.view(torch.int16).numpy().view(np.uint16).astype(np.uint32)
+        t = (w ^ r) if transform == "xor" else (w + r) & 0xFFFF
+        b_t = torch.from_numpy(t.astype(np.uint16).view(np.int16)).view(torch.bfloat16)
+    a, b = {"w": a_t}, {"w": b_t.clone()}
+    if odd:
+        a["u"] = a_t.view(torch.uint8)[: 2 * n - 1].clone()
+        b["u"] = b_t.view(torch.uint8)[: 2 * n - 1].clone()
+    return a, b
+
+
+def _fuzz_strategies() -> dict:
+    from hypothesis import strategies as st
+
+    return dict(
+        size_class=st.sampled_from([(1, 8191), (8191, 8193), (8192, 32768), (32769, 300_000)]),  # words
+        kind=st.sampled_from(["noise", "alphabet", "sparse"]),
+        param=st.sampled_from([0.0, 0.001, 0.01, 0.03, 0.1, 0.3]),
+        transform=st.sampled_from(["xor", "u16"]),
+        odd=st.booleans(),
+        policy=st.sampled_from(["auto", "xor", "u16"]),
+        coding=st.sampled_from([(-1, -1), (6, 0), (100, -1), (100, 1)]),  # (dict_slack_pct, escapes)
+        seed=st.integers(0, 2**31 - 1),
+    )
+
+
+# Hypothesis strategies of the property tests (random_pair's arguments, policy, coding).
+FUZZ = _fuzz_strategies()
+
+
 def host_plan(a: dict[str, torch.Tensor], b: dict[str, torch.Tensor], policy: str, threads: int = 4, dict_slack_pct: int = 6,
               escapes: int = 0):
     """Build a plan on host targets (no GPU); b's tensors are the destinations."""
