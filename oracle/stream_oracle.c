@@ -2,9 +2,9 @@
  * ORACLE — test infrastructure only, never part of the product path.
  *
  * Plain-C, single-threaded-per-block restatement of this project's delta
- * stream format (chunked, interleaved rANS; see the "Stream format" section
- * of the design notes), written independently of the product encoder and the
- * CUDA kernel. Used by tests/ to check (a) that the host encoder's output
+ * stream format (chunked, interleaved rANS; constants and descriptor layouts
+ * in warpshift_b200/csrc/ws_format.h), written independently of the product
+ * encoder and the CUDA kernel. Used by tests/ to check (a) that the host encoder's output
  * decodes to the exact residual and (b) that the GPU applied the same bytes,
  * and by bench.py's CPU baseline leg. Parity of the entropy stage against the
  * reference is unpinned: the reference codes with nvCOMP ANS (closed source),
