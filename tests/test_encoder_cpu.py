@@ -112,6 +112,26 @@ def test_dictionary_and_escape_limits_are_exact(adversarial, policy: str, suffix
         _lib.load().ws_plan_destroy(plan)
 
 
+def test_plans_do_not_depend_on_the_thread_count() -> None:
+    """The host encoder's plan is a function of the bytes alone: 1 and 7 threads
+    give identical descriptors, tables, arena and checksums (the GPU encoder is
+    checked against this plan byte for byte)."""
+    a, b = edge_pair(seed=14)
+    plans = [host_plan(a, clone(b), "auto", threads=t, escapes=0) for t in (1, 7)]
+    try:
+        (b1, t1, tab1, ar1, s1), (b7, t7, tab7, ar7, s7) = (plan_arrays(p) for p in plans)
+        for field in ("src", "nbytes", "clen", "nwords", "kind", "tail", "flags"):
+            np.testing.assert_array_equal(b1[field], b7[field], err_msg=field)
+        np.testing.assert_array_equal(t1.view(np.uint8), t7.view(np.uint8))
+        np.testing.assert_array_equal(tab1, tab7)
+        np.testing.assert_array_equal(ar1, ar7)
+        assert list(s1.expected_checksum) == list(s7.expected_checksum)
+        assert list(s1.mode_counts) == list(s7.mode_counts)
+    finally:
+        for p in plans:
+            _lib.load().ws_plan_destroy(p)
+
+
 def test_mode_rule_follows_the_reference() -> None:
     """delta.py:176-194: <16384 B raw, unchanged SKIP, odd sizes XOR_ANS, XOR-only policy never U16."""
     a, b = edge_pair(seed=8)
