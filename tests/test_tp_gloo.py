@@ -5,7 +5,9 @@ agreement of weights.py:106-137 on the CPU group, plus the checksum
 confirmation all-reduce (DeltaWeights.confirm) on the "device" group, which is
 NCCL in production and gloo here. Failures are injected on the host: a rank
 whose apply raises, a rank whose written bytes do not hash to the expected
-checksum, a rank with a stale source model.
+checksum, a rank with a stale source model. When the switch is not confirmed
+on every rank, the ranks whose own switch succeeded switch back, so every rank
+ends on the source model.
 """
 
 from __future__ import annotations
@@ -134,5 +136,6 @@ def test_two_ranks_agree_before_writing_and_confirm_after(scenario: str) -> None
         else:
             assert outcome.startswith("error") and "rank 1" in outcome
             assert current == "b"  # identity not committed on any rank
+            assert weight == 2.0 + rank  # every rank holds the source model again
     if scenario == "checksum_mismatch":
         assert "not confirmed" in results[0][0]

@@ -5,7 +5,7 @@ gpu_target)``, ``.apply(reverse)``, ``.validate_bindings()``, ``.bindings``,
 ``.device``, ``.stats`` and the module helpers ``_u16_residual`` and
 ``_batch_layout``. Underneath, nvCOMP and the Triton ``_restore_batch`` kernel
 are replaced by ``libwarpshift_b200.so``: a GPU encoder for prepare (statistics,
-rANS encode and packing kernels; host encoder threads as fallback) and one fused
+rANS encode and packing kernels; host encoder threads only on request) and one fused
 sm_100a decode+apply kernel per staging batch for apply.
 
 Per-packet mode choice keeps the reference rule (delta.py:176-194: raw XOR, then
@@ -86,9 +86,12 @@ class DeltaWeights:
     ``batch_bytes`` (bound on one H2D staging batch), ``staging_slots``,
     ``dict_slack_pct`` (word-dictionary coding when within this many percent of
     the byte planes' size; negative = never), ``encode_on_device`` (prepare on
-    the GPU), ``encode_batch_bytes`` (GPU encoder batch; 0 = 512 MiB) and
+    the GPU), ``encode_batch_bytes`` (GPU encoder batch; 0 = 512 MiB),
     ``escapes`` (dictionaries with escape lists: 0 when smaller, -1 never, 1
-    whenever eligible). ``save`` / ``load`` persist a package across restarts.
+    whenever eligible) and ``host_fallback`` (when the GPU encoder cannot get
+    its device buffers, encode on host threads instead of raising
+    RuntimeError; off by default). ``save`` / ``load`` persist a package
+    across restarts.
     """
 
     def __init__(
@@ -104,6 +107,7 @@ class DeltaWeights:
         encode_on_device: bool = True,
         encode_batch_bytes: int = 0,
         escapes: int = 0,
+        host_fallback: bool = False,
     ) -> None:
         started = time.perf_counter()
         if policy not in _lib.POLICIES:
@@ -136,6 +140,7 @@ class DeltaWeights:
             encode_on_device=int(bool(encode_on_device)),
             encode_batch_bytes=encode_batch_bytes,
             escapes=escapes,
+            host_fallback=int(bool(host_fallback)),
         )
         plan = ctypes.c_void_p()
         with torch.cuda.device(self.device):
@@ -283,6 +288,10 @@ class DeltaWeights:
         Raises RuntimeError if the device reports a corrupt frame or if the
         written bytes do not hash to the checksum recorded at prepare (for
         example when the resident weights were not the expected source model).
+        Before raising, the library rolls the switch back by applying the other
+        direction over the same stream; ``last_apply["rollback"]`` is
+        "restored" when the restored bytes hash to the source model's checksum
+        (see ``include/warpshift_b200.h``, ``WS_ROLLBACK_*``).
         """
         self.validate_bindings()
         caller_stream = torch.cuda.current_stream(self.device)
@@ -304,28 +313,30 @@ class DeltaWeights:
             "device_errors": int(result.device_errors),
             "h2d_bytes": int(result.h2d_bytes),
             "launches": int(result.launches),
+            "rollback": _lib.ROLLBACK.get(int(result.rollback), "unknown"),
         }
         _lib.check(rc)
 
-    def confirm(self, group: Any = None) -> dict[str, int]:
-        """All-reduce this rank's last apply outcome over ``group`` (NCCL in production).
+    def confirm(self, group: Any = None, failed: bool = False) -> dict[str, int]:
+        """All-reduce one success flag per rank over ``group`` (NCCL in production).
 
-        Sums, across ranks, a failure count and the written/expected checksums
-        (64-bit wraparound) so every rank learns whether the whole switch was
-        confirmed. Raises RuntimeError when any rank failed.
+        This rank's flag is up when its last apply succeeded, the bytes it wrote
+        hash to the checksum recorded at prepare, and ``failed`` is false.
+        Counting flags (rather than summing checksums, whose errors on two ranks
+        could cancel) tells every rank whether the whole switch happened. Raises
+        RuntimeError naming how many ranks failed.
         """
         import torch.distributed as dist
 
-        last = self.last_apply or {"ok": False, "checksum": 0, "expected": 0}
-        values = [0 if last["ok"] else 1, _as_int64(last["checksum"]), _as_int64(last["expected"])]
+        last = self.last_apply or {}
+        ok = not failed and bool(last.get("ok")) and last.get("checksum") == last.get("expected")
         on_device = dist.get_backend(group) == "nccl"
-        tensor = torch.tensor(values, dtype=torch.int64, device=self.device if on_device else "cpu")
-        dist.all_reduce(tensor, group=group)
-        failed, checksum, expected = (int(v) for v in tensor.tolist())
-        summary = {"failed_ranks": failed, "checksum": checksum & (2**64 - 1), "expected": expected & (2**64 - 1)}
-        if failed or summary["checksum"] != summary["expected"]:
-            raise RuntimeError(f"Delta switch not confirmed: {failed} rank(s) failed")
-        return summary
+        flags = torch.tensor([0 if ok else 1, 1], dtype=torch.int64, device=self.device if on_device else "cpu")
+        dist.all_reduce(flags, group=group)
+        failed_ranks, ranks = (int(v) for v in flags.tolist())
+        if failed_ranks:
+            raise RuntimeError(f"Delta switch not confirmed: {failed_ranks} of {ranks} rank(s) failed")
+        return {"failed_ranks": 0, "ranks": ranks}
 
     def set_resident(self, resident: bool) -> None:
         """Keep the whole encoded stream in HBM (applies then skip the H2D staging)."""
@@ -371,7 +382,3 @@ class DeltaWeights:
         except Exception:
             pass
 
-
-def _as_int64(value: int) -> int:
-    value &= 2**64 - 1
-    return value - 2**64 if value >= 2**63 else value
