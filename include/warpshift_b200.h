@@ -70,7 +70,9 @@ typedef struct ws_build_options {
                                   device holds up to about 4x this in temporary buffers during prepare */
   int32_t escapes;          /* word dictionaries with escapes (rare words listed after each block's
                                stream): 0 when estimated smaller, < 0 never, > 0 whenever eligible */
-  int32_t reserved;
+  int32_t host_fallback;    /* 1: when the GPU encoder cannot get its device buffers even with 32 MiB
+                               batches, encode on host threads instead; 0 (default): fail with
+                               WS_ERR_NOMEM */
 } ws_build_options;
 
 typedef struct ws_plan_stats {
@@ -101,9 +103,14 @@ typedef struct ws_apply_result {
   uint32_t device_errors;    /* OR of device error bits (see ws_format.h WS_DEVERR_*) */
   uint32_t bad_block_plus1;  /* 1 + index of a failing block, 0 if none */
   uint64_t h2d_bytes;        /* bytes copied host->device by this apply */
-  uint32_t launches;         /* decode kernel launches issued */
-  uint32_t reserved;
+  uint32_t launches;         /* decode kernel launches issued (a rollback's included) */
+  uint32_t rollback;         /* WS_ROLLBACK_*: what ws_apply did after a failed switch */
 } ws_apply_result;
+
+#define WS_ROLLBACK_NONE 0       /* the switch succeeded, or no rollback was attempted */
+#define WS_ROLLBACK_RESTORED 1   /* the inverse pass restored the source model (checksum verified) */
+#define WS_ROLLBACK_UNVERIFIED 2 /* the inverse pass ran; its bytes do not hash to the source model's */
+#define WS_ROLLBACK_FAILED 3     /* the inverse pass could not run or gave up: weights are undefined */
 
 /* Host-side view of a built plan, for checkers and CPU baselines. */
 typedef struct ws_plan_view {
@@ -138,9 +145,10 @@ WS_API int ws_u16_residual(const uint8_t* base, const uint8_t* target, uint64_t 
  * encoded on the device on `stream`; the payloads come back into the host arena and
  * the temporary device buffers are freed before returning. If the device cannot
  * hold the encoder's buffers, the GPU encoder retries with batches 4x smaller (down
- * to 32 MiB) and then falls back to the host encoder; ws_plan_stats.encoder says
- * which ran. Otherwise B is copied device->host in 16 MiB packets and encoded on
- * `threads` host threads. Both encoders produce byte-identical plans. */
+ * to 32 MiB); if that still fails, the build returns WS_ERR_NOMEM, or, only with
+ * opts->host_fallback, hands over to the host encoder (ws_plan_stats.encoder says
+ * which ran). Without encode_on_device, B is copied device->host in 16 MiB packets
+ * and encoded on `threads` host threads. Both encoders produce byte-identical plans. */
 WS_API int ws_plan_build(const ws_tensor_desc* tensors, uint64_t ntensors, const ws_build_options* opts,
                   void* stream, ws_plan** out);
 
@@ -158,7 +166,11 @@ WS_API int ws_plan_set_resident(ws_plan* plan, int resident, void* stream);
  * decodes and applies the batches alternately on compute_stream and a second
  * stream of the plan that compute_stream joins at the end, reads back the device
  * result, and returns after compute_stream completes. Returns WS_ERR_DEVICE or
- * WS_ERR_CHECKSUM on failure. */
+ * WS_ERR_CHECKSUM on failure, after rolling the switch back: the other direction
+ * is applied over the same stream, which writes back exactly the bytes that were
+ * resident, and the restored bytes are checked against the source model's
+ * checksum; out->rollback and the error message say how that went. The
+ * reference has no rollback (its server latches a failure, server.py:88-99). */
 WS_API int ws_apply(ws_plan* plan, int reverse, void* compute_stream, void* copy_stream, ws_apply_result* out);
 
 /* Asynchronous halves of ws_apply: enqueue only (no host synchronisation), then
@@ -176,20 +188,31 @@ WS_API int ws_plan_get_view(const ws_plan* plan, ws_plan_view* out);
  * free HBM, or one that routes every device allocation through its own
  * allocator). The caller passes, in device memory on `device`, the tile and
  * block descriptors and slot tables of a plan (layouts of ws_plan_get_view) and
- * the whole payload arena (block `src` offsets are relative to `payload`); the
- * weights named by the block descriptors are written in place and `out`
- * receives the checksum and device errors (`out->expected` stays 0: compare
- * with ws_plan_stats.expected_checksum). Its only scratch is a fixed
- * 16-byte-per-tile device array of WS_NOALLOC_MAX_TILES + 1 slots (256 KiB)
- * inside the library, held by every GPU that loads the library until exit; more
- * than WS_NOALLOC_MAX_TILES tiles per call is rejected with WS_ERR_INVALID.
- * The first call on a device looks up that array's device address (module
- * set-up), so make it before any stream capture. All calls on a device share the
+ * the whole payload arena (block `src` offsets are relative to `payload`), with
+ * the element counts of each array and the arena's byte size. `tiles`, `blocks`
+ * and `payload` must be 16-byte aligned and `tables` 4-byte aligned (else
+ * WS_ERR_INVALID). On the device every tile and block descriptor is checked
+ * against those sizes before it is followed (block range and table index of a
+ * tile; payload range, 16-byte alignment, byte count and kind of a block): one
+ * outside them is skipped and reported as device error WS_DEVERR_BOUNDS (16),
+ * with the call returning WS_ERR_DEVICE. The weights named by the block
+ * descriptors' `dst` are written in place; those addresses are the caller's
+ * and cannot be checked. `out` receives the checksum and device errors
+ * (`out->expected` stays 0: compare with ws_plan_stats.expected_checksum). Its
+ * only scratch is a fixed 16-byte-per-tile device array of
+ * WS_NOALLOC_MAX_TILES + 1 slots (256 KiB) inside the library, held by every
+ * GPU that loads the library until exit; more than WS_NOALLOC_MAX_TILES tiles
+ * per call is rejected with WS_ERR_INVALID. The first call on a device looks up
+ * that array's device address (module set-up). All calls on a device share the
  * array: calls that overlap on the GPU race and must be serialised by the
- * caller. Synchronous: returns after `stream` completes. */
+ * caller. The call is synchronous: it reads its result back to the host and
+ * returns after `stream` completes, so it cannot be made while `stream` is
+ * being captured into a CUDA graph. */
 #define WS_NOALLOC_MAX_TILES 16384
-WS_API int ws_apply_device_noalloc(const void* tiles, uint32_t ntiles, const void* blocks, const uint32_t* tables,
-                                   const void* payload, int reverse, int device, void* stream, ws_apply_result* out);
+WS_API int ws_apply_device_noalloc(const void* tiles, uint32_t ntiles, const void* blocks, uint32_t nblocks,
+                                   const uint32_t* tables, uint32_t ntables, const void* payload,
+                                   uint64_t payload_bytes, int reverse, int device, void* stream,
+                                   ws_apply_result* out);
 
 /* No counterpart in the reference, which prepares the delta again after every
  * restart (README.md:41). Writes a built plan to `path` (via `path`.tmp, then

@@ -20,7 +20,8 @@ from warpshift_b200 import _lib
 pytestmark = pytest.mark.gpu
 
 
-def build(a, b_dev, policy, slack, on_device, encode_batch_bytes=0, pin_arena=0, batch_bytes=0, escapes=0):
+def build(a, b_dev, policy, slack, on_device, encode_batch_bytes=0, pin_arena=0, batch_bytes=0, escapes=0,
+          host_fallback=0):
     lib = _lib.load()
     descs = (_lib.TensorDesc * len(a))()
     for i, name in enumerate(b_dev):
@@ -30,7 +31,7 @@ def build(a, b_dev, policy, slack, on_device, encode_batch_bytes=0, pin_arena=0,
     opts = _lib.BuildOptions(policy=_lib.POLICIES[policy], threads=4, target_on_device=1, device=0,
                              batch_bytes=batch_bytes, staging_slots=0, pin_arena=pin_arena, dict_slack_pct=slack,
                              encode_on_device=int(on_device), encode_batch_bytes=encode_batch_bytes,
-                             escapes=escapes)
+                             escapes=escapes, host_fallback=host_fallback)
     plan = ctypes.c_void_p()
     stream = torch.cuda.current_stream().cuda_stream
     _lib.check(lib.ws_plan_build(descs, len(a), ctypes.byref(opts), stream, ctypes.byref(plan)))
@@ -169,14 +170,18 @@ def fill_device(cuda_device, leave: int) -> list:
 @pytest.mark.parametrize("leave_mb, encoder", [(190, "gpu"), (60, "host")])
 def test_gpu_encoder_under_memory_pressure(cuda_device, leave_mb: int, encoder: str) -> None:
     """With little free HBM the GPU encoder retries with smaller batches (512 ->
-    128 -> 32 MiB), then hands over to the host encoder; the plan is the same."""
+    128 -> 32 MiB); below that the build fails with WS_ERR_NOMEM unless the host
+    encoder was allowed to take over. Either encoder gives the same plan."""
     x, y = bf16_pair((96 << 20) // 2, 0.01, 31)
     b_dev = {"w": y.to(cuda_device)}
     lib = _lib.load()
     p_host = build({"w": x}, b_dev, "auto", 6, False)
     held = fill_device(cuda_device, leave_mb << 20)
     try:
-        p_gpu = build({"w": x}, b_dev, "auto", 6, True)
+        if encoder == "host":
+            with pytest.raises(RuntimeError, match="host_fallback"):
+                build({"w": x}, b_dev, "auto", 6, True)
+        p_gpu = build({"w": x}, b_dev, "auto", 6, True, host_fallback=int(encoder == "host"))
     finally:
         del held
         torch.cuda.empty_cache()

@@ -37,7 +37,7 @@ class BuildOptions(ctypes.Structure):
         ("encode_on_device", i32),
         ("encode_batch_bytes", u64),
         ("escapes", i32),
-        ("reserved", i32),
+        ("host_fallback", i32),
     ]
 
 
@@ -72,8 +72,11 @@ class ApplyResult(ctypes.Structure):
         ("bad_block_plus1", u32),
         ("h2d_bytes", u64),
         ("launches", u32),
-        ("reserved", u32),
+        ("rollback", u32),
     ]
+
+
+ROLLBACK = {0: "none", 1: "restored", 2: "unverified", 3: "failed"}
 
 
 class PlanView(ctypes.Structure):
@@ -103,13 +106,14 @@ SIGNATURES = {
     "ws_plan_get_stats": ([P, ctypes.POINTER(PlanStats)], ctypes.c_int),
     "ws_plan_get_view": ([P, ctypes.POINTER(PlanView)], ctypes.c_int),
     "ws_plan_destroy": ([P], None),
-    "ws_apply_device_noalloc": ([P, u32, P, P, P, ctypes.c_int, ctypes.c_int, P, ctypes.POINTER(ApplyResult)], ctypes.c_int),
+    "ws_apply_device_noalloc": ([P, u32, P, u32, P, u32, P, u64, ctypes.c_int, ctypes.c_int, P, ctypes.POINTER(ApplyResult)], ctypes.c_int),
     "ws_plan_save": ([P, ctypes.c_char_p], ctypes.c_int),
     "ws_plan_load": ([ctypes.c_char_p, ctypes.POINTER(TensorDesc), u64, ctypes.POINTER(BuildOptions), ctypes.POINTER(P)], ctypes.c_int),
     "ws_selftest_wait_timeout": ([u32, ctypes.c_int, P, ctypes.POINTER(u32)], ctypes.c_int),
     "ws_tensor_hashes": ([ctypes.POINTER(P), ctypes.POINTER(u64), u64, ctypes.c_int, P, ctypes.POINTER(u64)], ctypes.c_int),
 }
 WS_NOALLOC_MAX_TILES = 16384
+WS_DEVERR_BOUNDS = 16
 ENCODERS = {0: "host", 1: "gpu", 2: "loaded"}
 
 _lock = threading.Lock()

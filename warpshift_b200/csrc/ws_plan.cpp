@@ -166,7 +166,8 @@ int encode_all(const ws_tensor_desc* tensors, const std::vector<PacketRef>& pack
                                       pr.nbytes, t.is_bf16 != 0});
     }
     // A serving process may have given most free HBM to its KV cache: on a device
-    // allocation failure retry with smaller batches, then use the host encoder.
+    // allocation failure retry with smaller batches; the host encoder takes over
+    // only when the caller allowed it.
     for (uint64_t batch = o.encode_batch_bytes ? o.encode_batch_bytes : (512ull << 20);; batch /= 4) {
       std::string err;
       bool oom = false;
@@ -181,6 +182,10 @@ int encode_all(const ws_tensor_desc* tensors, const std::vector<PacketRef>& pack
       cudaGetLastError();  // allocation failures are not sticky; clear the record
       if (batch / 4 < (32ull << 20)) break;
     }
+    if (!o.host_fallback)
+      return fail(WS_ERR_NOMEM,
+                  "GPU encoder: not enough free device memory for its buffers, even with 32 MiB batches (free "
+                  "device memory, or allow the host encoder with host_fallback)");
   }
   if (!o.target_on_device) {
     parallel_for(packets.size(), threads, [&](uint64_t i) {
@@ -709,10 +714,51 @@ int ws_apply_finish(ws_plan* p, void* compute_stream, ws_apply_result* out) {
   return ws::guarded([&] { return ws_apply_finish_impl(p, compute_stream, out); });
 }
 
-int ws_apply(ws_plan* p, int reverse, void* compute_stream, void* copy_stream, ws_apply_result* out) {
-  int rc = ws_apply_async(p, reverse, compute_stream, copy_stream);
+// A failed switch (corrupt stream or a checksum mismatch) has already written
+// every block it decoded. Both applies are exact inverses of each other (XOR is
+// its own inverse; the U16 directions add and subtract the same word), and the
+// decode of a block depends only on its payload bytes, so running the other
+// direction over the same stream writes back exactly the bytes that were
+// resident, corrupt blocks included. The restored bytes are then hashed like
+// any apply and compared with the checksum recorded at prepare for the source
+// model. A decode that gave up on a staging wait is not exactly repeatable and
+// its rollback is reported as unverified.
+static int ws_apply_impl(ws_plan* p, int reverse, void* compute_stream, void* copy_stream, ws_apply_result* out) {
+  int rc = ws_apply_async_impl(p, reverse, compute_stream, copy_stream);
   if (rc != WS_OK) return rc;
-  return ws_apply_finish(p, compute_stream, out);
+  ws_apply_result r{};
+  rc = ws_apply_finish_impl(p, compute_stream, &r);
+  if (rc == WS_ERR_DEVICE || rc == WS_ERR_CHECKSUM) {
+    const std::string first = g_last_error;
+    const int back_dir = reverse ? 0 : 1;
+    ws_apply_result back{};
+    int rb = ws_apply_async_impl(p, back_dir, compute_stream, copy_stream);
+    if (rb == WS_OK) rb = ws_apply_finish_impl(p, compute_stream, &back);
+    const char* how;
+    if (rb != WS_OK && rb != WS_ERR_DEVICE && rb != WS_ERR_CHECKSUM) {
+      r.rollback = WS_ROLLBACK_FAILED;
+      how = "; rollback failed: weights are undefined";
+    } else if ((back.device_errors & WS_DEVERR_TIMEOUT) || (r.device_errors & WS_DEVERR_TIMEOUT)) {
+      r.rollback = WS_ROLLBACK_FAILED;
+      how = "; rollback ran but a decode gave up on a staging wait: weights are undefined";
+    } else if (back.checksum == p->stats.expected_checksum[back_dir]) {
+      r.rollback = WS_ROLLBACK_RESTORED;
+      how = "; rolled back: the source model's bytes are restored (checksum verified)";
+    } else {
+      r.rollback = WS_ROLLBACK_UNVERIFIED;
+      how = "; rolled back, but the restored bytes do not hash to the source model's (the resident weights were "
+            "not the package's source model)";
+    }
+    r.h2d_bytes += back.h2d_bytes;
+    r.launches += back.launches;
+    fail(rc, first + how);
+  }
+  if (out) *out = r;
+  return rc;
+}
+
+int ws_apply(ws_plan* p, int reverse, void* compute_stream, void* copy_stream, ws_apply_result* out) {
+  return ws::guarded([&] { return ws_apply_impl(p, reverse, compute_stream, copy_stream, out); });
 }
 
 int ws_plan_get_stats(const ws_plan* p, ws_plan_stats* out) {
