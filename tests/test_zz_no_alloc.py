@@ -7,8 +7,10 @@ exposes one entry point that takes descriptors, tables and payload already in
 the caller's device memory and keeps its only scratch in a fixed device array
 inside the library. This file checks, through the C ABI, that two calls in a
 row write exactly the bytes (and report exactly the checksum) of the plan-based
-entry point ws_apply, that the second call changes no free device memory, and
-that oversized requests are rejected. Bytes are compared bit-exactly, as in
+entry point ws_apply, that the second call changes no free device memory, that
+oversized requests are rejected, that a corrupt block comes back as a device
+error naming it, and that descriptors pointing outside the caller's arrays are
+refused on the device without being followed. Bytes are compared bit-exactly, as in
 every parity test of this repository. The file is named so pytest collects it
 last.
 """
@@ -48,21 +50,26 @@ def build_device_plan(a, targets, device):
         "tables": torch.from_numpy(tables.copy() if tables.size else np.zeros(1, np.uint32)).view(torch.int32).to(device),
         "payload": torch.from_numpy(arena.copy() if arena.size else np.zeros(16, np.uint8)).to(device),
         "ntiles": int(tiles.size),
+        "nblocks": int(blocks.size),
+        "ntables": int(tables.size // 512),
+        "host_blocks": blocks.copy(),
+        "host_tiles": tiles.copy(),
         "expected": (int(stats.expected_checksum[0]), int(stats.expected_checksum[1])),
     }
     lib.ws_plan_destroy(plan)
     return dev
 
 
-def call_noalloc(dev, reverse: bool, device) -> _lib.ApplyResult:
+def call_noalloc(dev, reverse: bool, device, check: bool = True) -> tuple[int, _lib.ApplyResult]:
     result = _lib.ApplyResult()
     rc = _lib.load().ws_apply_device_noalloc(
-        dev["tiles"].data_ptr(), dev["ntiles"], dev["blocks"].data_ptr(), dev["tables"].data_ptr(),
-        dev["payload"].data_ptr(), int(reverse), device.index, torch.cuda.current_stream(device).cuda_stream,
-        ctypes.byref(result),
+        dev["tiles"].data_ptr(), dev["ntiles"], dev["blocks"].data_ptr(), dev["nblocks"], dev["tables"].data_ptr(),
+        dev["ntables"], dev["payload"].data_ptr(), dev["payload"].numel(), int(reverse), device.index,
+        torch.cuda.current_stream(device).cuda_stream, ctypes.byref(result),
     )
-    _lib.check(rc)
-    return result
+    if check:
+        _lib.check(rc)
+    return rc, result
 
 
 def test_noalloc_matches_plan_apply_on_two_calls(cuda_device) -> None:
@@ -76,7 +83,7 @@ def test_noalloc_matches_plan_apply_on_two_calls(cuda_device) -> None:
         delta.apply(reverse=reverse)
         torch.cuda.synchronize(cuda_device)
         free_before = torch.cuda.mem_get_info(cuda_device)[0]
-        result = call_noalloc(dev, reverse, cuda_device)
+        _, result = call_noalloc(dev, reverse, cuda_device)
         free_after = torch.cuda.mem_get_info(cuda_device)[0]
         if call == 1:  # the first call may load the module's fixed array; later calls allocate nothing
             assert free_after == free_before
@@ -92,8 +99,66 @@ def test_noalloc_rejects_more_tiles_than_its_fixed_scratch(cuda_device) -> None:
     dummy = torch.zeros(64, dtype=torch.uint8, device=cuda_device)
     result = _lib.ApplyResult()
     rc = _lib.load().ws_apply_device_noalloc(
-        dummy.data_ptr(), _lib.WS_NOALLOC_MAX_TILES + 1, dummy.data_ptr(), dummy.data_ptr(), dummy.data_ptr(), 0,
-        cuda_device.index, torch.cuda.current_stream(cuda_device).cuda_stream, ctypes.byref(result),
+        dummy.data_ptr(), _lib.WS_NOALLOC_MAX_TILES + 1, dummy.data_ptr(), 1, dummy.data_ptr(), 1, dummy.data_ptr(), 64,
+        0, cuda_device.index, torch.cuda.current_stream(cuda_device).cuda_stream, ctypes.byref(result),
     )
     assert rc == _lib.WS_ERR_INVALID
     assert "exceed the maximum" in _lib.last_error()
+
+
+def test_noalloc_reports_a_corrupt_block_with_its_index(cuda_device) -> None:
+    """A flipped payload byte of one coded block comes back as a device error
+    naming that block, through the per-tile slots and their reduction."""
+    a, b = edge_pair(seed=22, big=False)
+    targets = {k: v.to(cuda_device) for k, v in b.items()}
+    dev = build_device_plan(a, targets, cuda_device)
+    coded = [i for i, bk in enumerate(dev["host_blocks"]) if bk["kind"] != 0 and bk["clen"] > 1024]
+    assert coded
+    victim = coded[len(coded) // 2]
+    bk = dev["host_blocks"][victim]
+    spot = int(bk["src"]) + 256 + (2 * int(bk["nwords"]) - 256) // 2
+    dev["payload"][spot] ^= 0x3C
+    rc, result = call_noalloc(dev, True, cuda_device, check=False)
+    assert rc == _lib.WS_ERR_DEVICE
+    assert result.device_errors & 3 and result.bad_block_plus1 == victim + 1
+    assert "corrupt block" in _lib.last_error()
+
+
+@pytest.mark.parametrize("field", ["tile_first_block", "block_src", "block_src_misaligned", "tile_table"])
+def test_noalloc_refuses_descriptors_outside_the_arrays(cuda_device, field: str) -> None:
+    """Caller-written descriptors that point outside the given arrays are
+    reported as WS_DEVERR_BOUNDS and never followed: the weights stay as they were."""
+    a, b = edge_pair(seed=23, big=False)
+    targets = {k: v.to(cuda_device) for k, v in b.items()}
+    dev = build_device_plan(a, targets, cuda_device)
+    before = {k: as_bytes(v).copy() for k, v in targets.items()}
+    tiles, blocks = dev["host_tiles"].copy(), dev["host_blocks"].copy()
+    coded_tile = next(i for i, t in enumerate(tiles) if t["table"] != 0xFFFFFFFF)
+    if field == "tile_first_block":
+        tiles[0]["first_block"] = dev["nblocks"]
+    elif field == "tile_table":
+        tiles[coded_tile]["table"] = dev["ntables"]
+    elif field == "block_src":
+        blocks[0]["src"] = dev["payload"].numel() - 16
+        blocks[0]["clen"] = max(32, int(blocks[0]["clen"]))
+    else:
+        blocks[0]["src"] = int(blocks[0]["src"]) + 8
+    dev["tiles"] = torch.from_numpy(tiles.view(np.uint8).copy()).to(cuda_device)
+    dev["blocks"] = torch.from_numpy(blocks.view(np.uint8).copy()).to(cuda_device)
+    rc, result = call_noalloc(dev, True, cuda_device, check=False)
+    assert rc == _lib.WS_ERR_DEVICE
+    assert result.device_errors & _lib.WS_DEVERR_BOUNDS
+    assert "outside the given arrays" in _lib.last_error()
+    assert result.bad_block_plus1 >= 1
+    # The refused tile's blocks (or the refused block) were not written.
+    if field.startswith("tile"):
+        orig = dev["host_tiles"][coded_tile if field == "tile_table" else 0]
+        refused = range(int(orig["first_block"]), int(orig["first_block"]) + int(orig["nblocks"]))
+    else:
+        refused = [0]
+    bases = {n: t.data_ptr() for n, t in targets.items()}
+    for i in refused:
+        dst = int(dev["host_blocks"][i]["dst"])
+        owner = max((n for n in bases if bases[n] <= dst), key=lambda n: bases[n])
+        off, n = dst - bases[owner], int(dev["host_blocks"][i]["nbytes"])
+        np.testing.assert_array_equal(as_bytes(targets[owner])[off : off + n], before[owner][off : off + n])

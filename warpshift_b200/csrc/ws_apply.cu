@@ -40,6 +40,7 @@ constexpr uint32_t kSmemBytes = kBarOffset + kWarps * 2 * 8;
 constexpr uint32_t kRingHalfwords = WS_RING_BYTES / 2;      // 1024
 constexpr uint32_t kHalfHalfwords = WS_RING_HALF_BYTES / 2; // 512
 constexpr uint32_t kWaitLimit = 1u << 20;      // bounded spin on a staging barrier
+constexpr uint32_t kDrainRounds = 16;          // bounded waits per outstanding copy before a CTA exits
 constexpr uint32_t kPrefetchGroups = 3;        // destination groups requested into L2 ahead of their load
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -595,26 +596,62 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
       if (pos != bd.nwords || !escapes_ok) report(res, WS_DEVERR_LENGTH, block);
     }
   }
-  // Never leave a bulk copy in flight into shared memory of an exiting CTA.
-  while (ready < issued) {
-    if (!mbar_wait(bar_base + (ready & 1u) * 8u, (ready >> 1) & 1u)) {
+  // Never leave a bulk copy in flight into shared memory of an exiting CTA: the
+  // copies still outstanding (possible only after a timeout) get up to
+  // kDrainRounds further bounded waits in all. A copy from this GPU's own memory
+  // that has not landed after all of them means the memory system stopped
+  // answering.
+  for (uint32_t round = 0; ready < issued && round < kDrainRounds;) {
+    if (mbar_wait(bar_base + (ready & 1u) * 8u, (ready >> 1) & 1u)) {
+      ++ready;
+    } else {
+      ++round;
       if (lane == 0) report(res, WS_DEVERR_TIMEOUT, block);
-      break;
     }
-    ++ready;
   }
   ck.finish(lane, block, res);
 }
 
-template <bool REVERSE>
-__global__ void __launch_bounds__(kThreads, 2)
-    ws_apply_kernel(const ws_tile_desc* __restrict__ tiles, uint32_t tile_begin,
-                    const ws_block_desc* __restrict__ blocks, const uint32_t* __restrict__ tables,
-                    const uint8_t* __restrict__ payload, uint64_t payload_offset, ws_device_result* res) {
+// Bounds of the caller-owned arrays an allocation-free apply receives. The
+// plan-based apply builds its descriptors itself and runs unchecked.
+struct DescLimits {
+  uint32_t nblocks;
+  uint32_t ntables;
+  uint64_t payload_bytes;
+};
+
+// A block descriptor the kernel can follow without leaving the payload: a
+// 16-byte-aligned payload range inside the caller's arena (cp.async.bulk needs
+// 16-byte alignment), 1..65536 weight bytes, a known kind, and a raw payload
+// that holds every weight byte it XORs.
+__device__ __forceinline__ bool block_in_bounds(const ws_block_desc& bd, uint64_t payload_bytes) {
+  return (bd.src & 15u) == 0 && (bd.clen & 15u) == 0 && bd.src <= payload_bytes &&
+         bd.clen <= payload_bytes - bd.src && bd.nbytes >= 1 && bd.nbytes <= WS_BLOCK_BYTES &&
+         bd.kind <= WS_KIND_DICT_U16 && (bd.kind != WS_KIND_RAW || bd.nbytes <= bd.clen);
+}
+
+// The per-tile work shared by both apply kernels: expand the packet's tables
+// into the lane replicas, set up each warp's staging barriers, then one warp
+// per block of the tile. `payload` is the device address of arena byte
+// `payload_offset`. With CHECKED, every descriptor is first checked against
+// `lim`; one that points outside the caller's arrays is reported as
+// WS_DEVERR_BOUNDS and not followed.
+template <bool REVERSE, bool CHECKED>
+__device__ __forceinline__ void apply_tile(const ws_tile_desc& tile, const ws_block_desc* __restrict__ blocks,
+                                           const uint32_t* __restrict__ tables, const uint8_t* __restrict__ payload,
+                                           uint64_t payload_offset, ws_device_result* res, DescLimits lim) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint32_t* tbl = reinterpret_cast<uint32_t*>(smem);
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-  const ws_tile_desc tile = tiles[tile_begin + blockIdx.x];
+  if (CHECKED) {
+    // Uniform over the CTA: either every thread returns here or none does.
+    const bool tile_ok = tile.nblocks <= kWarps && (uint64_t)tile.first_block + tile.nblocks <= lim.nblocks &&
+                         (tile.table == WS_NO_TABLE || tile.table < lim.ntables);
+    if (!tile_ok) {
+      if (threadIdx.x == 0) report(res, WS_DEVERR_BOUNDS, tile.first_block);
+      return;
+    }
+  }
   if (tile.table != WS_NO_TABLE) {
     // Thread t expands slot entry t (plane t >> 8) into its 32 replicas; the
     // rotated segment order keeps 8 consecutive threads on distinct banks.
@@ -635,6 +672,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (warp >= tile.nblocks) return;
   const uint32_t block = tile.first_block + warp;
   const ws_block_desc bd = blocks[block];
+  if (CHECKED && (!block_in_bounds(bd, lim.payload_bytes) || (bd.kind != WS_KIND_RAW && tile.table == WS_NO_TABLE))) {
+    if (lane == 0) report(res, WS_DEVERR_BOUNDS, block);
+    return;
+  }
   const uint8_t* src = payload + (bd.src - payload_offset);
   uint8_t* ring = smem + kRingOffset + warp * kRingStride;
   switch (bd.kind) {
@@ -656,6 +697,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     default:
       if (lane == 0) report(res, WS_DEVERR_KIND, block);
   }
+}
+
+template <bool REVERSE>
+__global__ void __launch_bounds__(kThreads, 2)
+    ws_apply_kernel(const ws_tile_desc* __restrict__ tiles, uint32_t tile_begin,
+                    const ws_block_desc* __restrict__ blocks, const uint32_t* __restrict__ tables,
+                    const uint8_t* __restrict__ payload, uint64_t payload_offset, ws_device_result* res) {
+  apply_tile<REVERSE, false>(tiles[tile_begin + blockIdx.x], blocks, tables, payload, payload_offset, res,
+                             DescLimits{});
 }
 
 }  // namespace
@@ -706,57 +756,15 @@ static __device__ __align__(256) ws_device_result g_noalloc_scratch[WS_NOALLOC_M
 namespace ws {
 namespace {
 
-// Same per-tile work as ws_apply_kernel, but each tile accumulates into its own
+// Same per-tile work as ws_apply_kernel, with every caller-written descriptor
+// checked against the caller's array sizes; each tile accumulates into its own
 // scratch slot (slot = tile index) instead of one shared accumulator.
 template <bool REVERSE>
 __global__ void __launch_bounds__(kThreads, 2)
     ws_apply_noalloc_kernel(const ws_tile_desc* __restrict__ tiles, const ws_block_desc* __restrict__ blocks,
                             const uint32_t* __restrict__ tables, const uint8_t* __restrict__ payload,
-                            ws_device_result* scratch) {
-  extern __shared__ __align__(1024) uint8_t smem[];
-  uint32_t* tbl = reinterpret_cast<uint32_t*>(smem);
-  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-  const ws_tile_desc tile = tiles[blockIdx.x];
-  ws_device_result* res = scratch + blockIdx.x;
-  if (tile.table != WS_NO_TABLE) {
-    const uint32_t t = threadIdx.x;
-    const uint32_t e = __ldg(tables + (uint64_t)tile.table * 512u + t);
-    const uint4 v = make_uint4(e, e, e, e);
-    uint4* row = reinterpret_cast<uint4*>(tbl + (t >> 8) * kTableWords + (t & 255u) * 32u);
-#pragma unroll
-    for (uint32_t k = 0; k < 8; ++k) row[(k + t) & 7u] = v;
-  }
-  const uint32_t bar_base = smem_addr(smem + kBarOffset) + warp * 16u;
-  if (lane == 0) {
-    mbar_init(bar_base, 1);
-    mbar_init(bar_base + 8, 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-  if (warp >= tile.nblocks) return;
-  const uint32_t block = tile.first_block + warp;
-  const ws_block_desc bd = blocks[block];
-  const uint8_t* src = payload + bd.src;
-  uint8_t* ring = smem + kRingOffset + warp * kRingStride;
-  switch (bd.kind) {
-    case WS_KIND_RAW:
-      raw_block(bd, block, src, lane, res);
-      break;
-    case WS_KIND_ANS_XOR:
-      ans_block<false, REVERSE, false>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
-      break;
-    case WS_KIND_ANS_U16:
-      ans_block<true, REVERSE, false>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
-      break;
-    case WS_KIND_DICT_XOR:
-      ans_block<false, REVERSE, true>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
-      break;
-    case WS_KIND_DICT_U16:
-      ans_block<true, REVERSE, true>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
-      break;
-    default:
-      if (lane == 0) report(res, WS_DEVERR_KIND, block);
-  }
+                            DescLimits lim, ws_device_result* scratch) {
+  apply_tile<REVERSE, true>(tiles[blockIdx.x], blocks, tables, payload, 0, scratch + blockIdx.x, lim);
 }
 
 // Sums the per-tile slots [0, n) into slot WS_NOALLOC_MAX_TILES (one CTA).
@@ -813,27 +821,28 @@ int noalloc_scratch(int device, ws_device_result** out) {
 }  // namespace
 }  // namespace ws
 
-static int ws_apply_device_noalloc_impl(const void* tiles, uint32_t ntiles, const void* blocks,
-                                              const uint32_t* tables, const void* payload, int reverse, int device,
-                                              void* stream, ws_apply_result* out) {
+static int ws_apply_device_noalloc_impl(const void* tiles, uint32_t ntiles, const void* blocks, uint32_t nblocks,
+                                        const uint32_t* tables, uint32_t ntables, const void* payload,
+                                        uint64_t payload_bytes, int reverse, int device, void* stream,
+                                        ws_apply_result* out) {
   using namespace ws;
-  if (!out) {
-    set_last_error("ws_apply_device_noalloc: null result pointer");
+  auto reject = [](const std::string& why) {
+    set_last_error(("ws_apply_device_noalloc: " + why).c_str());
     return WS_ERR_INVALID;
-  }
+  };
+  if (!out) return reject("null result pointer");
   *out = ws_apply_result{};
   if (ntiles == 0) return WS_OK;
-  if (ntiles > WS_NOALLOC_MAX_TILES) {
-    set_last_error(("ws_apply_device_noalloc: " + std::to_string(ntiles) + " tiles exceed the maximum of " +
-                    std::to_string(WS_NOALLOC_MAX_TILES) +
-                    " per call (its per-tile results live in a fixed device array); split the tiles over several calls")
-                       .c_str());
-    return WS_ERR_INVALID;
-  }
-  if (!tiles || !blocks || !payload || device < 0 || device >= kMaxDevices) {
-    set_last_error("ws_apply_device_noalloc: null descriptor/payload pointer or bad device ordinal");
-    return WS_ERR_INVALID;
-  }
+  if (ntiles > WS_NOALLOC_MAX_TILES)
+    return reject(std::to_string(ntiles) + " tiles exceed the maximum of " + std::to_string(WS_NOALLOC_MAX_TILES) +
+                  " per call (its per-tile results live in a fixed device array); split the tiles over several calls");
+  if (!tiles || !blocks || !payload || nblocks == 0 || payload_bytes == 0)
+    return reject("null tile, block or payload array, or an empty block list or payload");
+  if (ntables && !tables) return reject("null table array with ntables > 0");
+  // cp.async.bulk stages payload bytes with 16-byte-aligned addresses; descriptors are read as 16-byte records.
+  if (((uintptr_t)tiles & 15u) || ((uintptr_t)blocks & 15u) || ((uintptr_t)payload & 15u) || ((uintptr_t)tables & 3u))
+    return reject("tiles, blocks and payload must be 16-byte aligned and tables 4-byte aligned");
+  if (device < 0 || device >= kMaxDevices) return reject("bad device ordinal " + std::to_string(device));
   int prev = -1;
   cudaGetDevice(&prev);
   auto done = [&](int rc) {
@@ -856,7 +865,8 @@ static int ws_apply_device_noalloc_impl(const void* tiles, uint32_t ntiles, cons
   if (e == cudaSuccess) {
     kernel<<<ntiles, kThreads, kSmemBytes, s>>>(static_cast<const ws_tile_desc*>(tiles),
                                                  static_cast<const ws_block_desc*>(blocks), tables,
-                                                 static_cast<const uint8_t*>(payload), scratch);
+                                                 static_cast<const uint8_t*>(payload),
+                                                 DescLimits{nblocks, ntables, payload_bytes}, scratch);
     e = cudaGetLastError();
   }
   if (e == cudaSuccess) {
@@ -876,16 +886,22 @@ static int ws_apply_device_noalloc_impl(const void* tiles, uint32_t ntiles, cons
   out->bad_block_plus1 = total.bad_block_plus1;
   out->launches = 2;
   if (total.errors) {
-    set_last_error("ws_apply_device_noalloc: device reported a corrupt block");
+    set_last_error((total.errors & WS_DEVERR_BOUNDS)
+                       ? "ws_apply_device_noalloc: a tile or block descriptor points outside the given arrays"
+                       : "ws_apply_device_noalloc: device reported a corrupt block");
     return done(WS_ERR_DEVICE);
   }
   return done(WS_OK);
 }
 
-extern "C" WS_API int ws_apply_device_noalloc(const void* tiles, uint32_t ntiles, const void* blocks,
-                                              const uint32_t* tables, const void* payload, int reverse, int device,
-                                              void* stream, ws_apply_result* out) {
-  return ws::guarded([&] { return ws_apply_device_noalloc_impl(tiles, ntiles, blocks, tables, payload, reverse, device, stream, out); });
+extern "C" WS_API int ws_apply_device_noalloc(const void* tiles, uint32_t ntiles, const void* blocks, uint32_t nblocks,
+                                              const uint32_t* tables, uint32_t ntables, const void* payload,
+                                              uint64_t payload_bytes, int reverse, int device, void* stream,
+                                              ws_apply_result* out) {
+  return ws::guarded([&] {
+    return ws_apply_device_noalloc_impl(tiles, ntiles, blocks, nblocks, tables, ntables, payload, payload_bytes,
+                                        reverse, device, stream, out);
+  });
 }
 
 // ---------------------------------------------------------------------------

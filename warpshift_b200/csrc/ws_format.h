@@ -75,6 +75,7 @@ enum ws_kind {
 #define WS_DEVERR_LENGTH 2u    // stream words consumed != nwords
 #define WS_DEVERR_TIMEOUT 4u   // a bounded wait on a staging barrier gave up
 #define WS_DEVERR_KIND 8u      // unknown block kind
+#define WS_DEVERR_BOUNDS 16u   // a caller-written descriptor points outside the caller's arrays (checked applies)
 
 // 32-byte block descriptor (resident in HBM for the plan's lifetime).
 typedef struct ws_block_desc {
