@@ -1,8 +1,8 @@
 """Generate golden vectors from the reference implementation itself.
 
-Run in a container that has the reference checkout (default /root/reference):
+Run in a container that has a checkout of the reference (its repository root):
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <path to the reference checkout>
 
 It imports the reference's ``warpshift.delta`` (no bytecode is written into the
 read-only checkout) and records, on seeded inputs:
@@ -31,7 +31,7 @@ HERE = Path(__file__).resolve().parent
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True, help="root of the reference checkout")
     args = parser.parse_args()
     os.environ["TRITON_INTERPRET"] = "1"
     sys.dont_write_bytecode = True
