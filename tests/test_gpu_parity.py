@@ -73,14 +73,19 @@ def test_boundary_residuals_round_trip_bit_exact(cuda_device, adversarial, polic
 @pytest.mark.parametrize("coding", list(CODINGS))
 @pytest.mark.parametrize("policy", ["xor", "u16"])
 def test_decoded_residual_matches_oracle(cuda_device, policy: str, coding: str) -> None:
-    """Apply onto zeroed weights: the kernel then writes the residual itself."""
+    """Apply onto zeroed weights: the kernel then writes the residual itself.
+
+    The asynchronous halves (apply_async + finish) are used because the
+    written bytes cannot match the checksum recorded at prepare, and the
+    synchronous apply would roll such a switch back."""
     a, b = edge_pair(seed=2, big=False)
     gpu = to_device(b, cuda_device)
     delta = DeltaWeights(a, gpu, policy=policy, dict_slack_pct=CODINGS[coding][0], escapes=CODINGS[coding][1])
     for t in gpu.values():
         t.zero_()
+    delta.apply_async(reverse=False)
     with pytest.raises(RuntimeError, match="checksum"):
-        delta.apply(reverse=False)
+        delta.finish()
     for name, t in gpu.items():
         base, target = as_bytes(a[name]), as_bytes(b[name])
         xor = sem.xor_residual(base, target)
@@ -158,6 +163,8 @@ def test_checksum_rejects_wrong_resident_model(cuda_device) -> None:
     with pytest.raises(RuntimeError, match="checksum"):
         delta.apply(reverse=True)  # weights already hold A: the written bytes are not A
     assert not delta.last_apply["ok"]
+    assert delta.last_apply["rollback"] == "unverified"  # rolled back onto what was resident: A
+    assert_bytes_equal(gpu, a)
 
 
 def test_misaligned_destinations(cuda_device) -> None:

@@ -31,8 +31,18 @@ namespace {
 
 constexpr uint32_t kWarps = WS_TILE_BLOCKS;
 constexpr uint32_t kThreads = kWarps * 32;
-constexpr uint32_t kTableWords = 256 * 32;                  // one replicated plane table
-constexpr uint32_t kRingOffset = 2 * kTableWords * 4;       // bytes
+// Replicated slot tables: row `slot` (256 bytes) holds plane 0's entry for lanes
+// 0..31 (bytes 4 * lane) and plane 1's (bytes 128 + 4 * lane), so lane l always
+// reads bank l, and a lookup address is one PRMT of the state (its low byte
+// moved into byte 1) over the lane's row offset, plus the table base.
+constexpr uint32_t kRowBytes = 256;
+constexpr uint32_t kTableBytes = 256 * kRowBytes;           // both planes, 64 KiB
+constexpr uint32_t kRingOffset = kTableBytes;               // bytes
+// Shared address at which the dynamic shared memory (and so the table region)
+// of a kernel without static shared variables begins on sm_100 (after the 1 KiB
+// the system reserves). The kernel checks it at run time and falls back to a
+// register base if it differs.
+constexpr uint32_t kFixedTableBase = 0x400;
 constexpr uint32_t kMirror = 640;  // a group reads <= 512 + 128 bytes past its start position
 constexpr uint32_t kRingStride = WS_RING_BYTES + kMirror;
 constexpr uint32_t kBarOffset = kRingOffset + kWarps * kRingStride;
@@ -231,8 +241,8 @@ __device__ void raw_block(const ws_block_desc& bd, uint32_t block, const uint8_t
 // planes, word = sym0 | sym1 << 8. Slot entry: bias | sym << 8 | freq << 16.
 #define WS_STEP_C(ea, eb)                                      \
   {                                                            \
-    ea = lds32(tb0 + ((xa & 255u) << 7));                      \
-    eb = lds32(tb1 + ((xb & 255u) << 7));                      \
+    ea = lds32(tb0 + ((xa & 255u) << 8));                      \
+    eb = lds32(tb1 + ((xb & 255u) << 8));                      \
     xa = (ea >> 16) * (xa >> 8) + (ea & 255u);                 \
     xb = (eb >> 16) * (xb >> 8) + (eb & 255u);                 \
   }
@@ -251,101 +261,121 @@ __device__ void raw_block(const ws_block_desc& bd, uint32_t block, const uint8_t
     pos += ca + __popc(bb);                                                                   \
   }
 
+// Row address of a slot entry: PRMT moves the state's low byte (the slot) into
+// byte 1 over the lane's row offset (byte 0), and the table region's base is
+// added. When the region sits at the expected shared address (FIXED_BASE) the
+// base is the load's immediate offset (operand %8) and costs no instruction;
+// otherwise it is added from a register.
+#define WS_ROW_ADDR(ADD) \
+  " prmt.b32 aa, %0, %5, 0x5504;\n prmt.b32 ab, %1, %6, 0x5504;\n" ADD
+#define WS_ROW_ADDR_D(ADD) \
+  " prmt.b32 aa, %0, %6, 0x5504;\n prmt.b32 ab, %1, %6, 0x5504;\n" ADD
+#define WS_ADD_BASE_F " add.u32 aa, aa, %4;\n add.u32 ab, ab, %4;\n"
+#define WS_ADD_BASE_D " add.u32 aa, aa, %5;\n add.u32 ab, ab, %5;\n"
+#define WS_LD_ENTRIES " ld.shared.u32 ea, [aa+%8];\n ld.shared.u32 eb, [ab+%8];\n"
+
+// Renormalisation shared by both checks: ballot, prefix counts, one 16-bit word
+// per state below 2^16 (plane-0 / even-word states first in lane order, then
+// the others, read from rb = rp + 2 * their count); XA, XB, RP, LTM name the
+// asm operands.
+#define WS_RENORM_PTX(XA, XB, RP, LTM)                                                             \
+  " setp.lt.u32 pa, " XA ", 65536;\n setp.lt.u32 pb, " XB ", 65536;\n"                              \
+  " vote.sync.ballot.b32 va, pa, 0xffffffff;\n vote.sync.ballot.b32 vb, pb, 0xffffffff;\n"           \
+  " popc.b32 ca, va;\n"                                                                             \
+  " and.b32 t, va, " LTM ";\n popc.b32 oa, t;\n mad.lo.u32 ada, oa, 2, " RP ";\n"                  \
+  " mad.lo.u32 rb, ca, 2, " RP ";\n"                                                                \
+  " and.b32 t, vb, " LTM ";\n popc.b32 ob, t;\n mad.lo.u32 adb, ob, 2, rb;\n"                      \
+  " popc.b32 cb, vb;\n mad.lo.u32 " RP ", cb, 2, rb;\n"                                            \
+  " @pa ld.shared.u16 wa, [ada];\n @pb ld.shared.u16 wb, [adb];\n"                                  \
+  " @pa prmt.b32 " XA ", wa, " XA ", 0x5410;\n @pb prmt.b32 " XB ", wb, " XB ", 0x5410;\n"
+
 // Fast-path check in hand-written PTX: two decode steps of both planes (the
 // lane's words 2c and 2c+1 of the group) and one renormalisation check.
 // rp is the byte address of the current stream position in the ring; the
-// caller re-bases it once per group. Returns the two words as lo | hi << 16.
-__device__ __forceinline__ uint32_t check_fast(uint32_t& xa, uint32_t& xb, uint32_t& rp, uint32_t tb0, uint32_t tb1,
-                                               uint32_t ltm) {
+// caller re-bases it once per group. `tbase` is the table region's shared
+// address and lba / lbb the lane's row offsets of planes 0 and 1. Returns the
+// two words as lo | hi << 16.
+#define WS_CHECK_FAST_PTX(ADD)                                                             \
+  "{\n"                                                                                    \
+  " .reg .u32 aa, ab, ea, eb, qa, qb, fa, fb, ba, bb, w0, w1, va, vb, ca, cb, oa, ob, t, rb, ada, adb, wa, wb;\n" \
+  " .reg .pred pa, pb;\n"                                                                  \
+  WS_ROW_ADDR(ADD)                                                                         \
+  WS_LD_ENTRIES                                                                            \
+  " shr.u32 qa, %0, 8;\n shr.u32 qb, %1, 8;\n"                                            \
+  " shr.u32 fa, ea, 16;\n shr.u32 fb, eb, 16;\n"                                          \
+  " and.b32 ba, ea, 255;\n and.b32 bb, eb, 255;\n"                                        \
+  " mad.lo.u32 %0, fa, qa, ba;\n mad.lo.u32 %1, fb, qb, bb;\n"                            \
+  " prmt.b32 w0, ea, eb, 0x0051;\n"                                                        \
+  WS_ROW_ADDR(ADD)                                                                         \
+  WS_LD_ENTRIES                                                                            \
+  " shr.u32 qa, %0, 8;\n shr.u32 qb, %1, 8;\n"                                            \
+  " shr.u32 fa, ea, 16;\n shr.u32 fb, eb, 16;\n"                                          \
+  " and.b32 ba, ea, 255;\n and.b32 bb, eb, 255;\n"                                        \
+  " mad.lo.u32 %0, fa, qa, ba;\n mad.lo.u32 %1, fb, qb, bb;\n"                            \
+  " prmt.b32 w1, ea, eb, 0x5100;\n"                                                        \
+  " prmt.b32 %2, w0, w1, 0x7610;\n"                                                        \
+  WS_RENORM_PTX("%0", "%1", "%3", "%7")                                                     \
+  "}\n"
+
+template <bool FIXED_BASE>
+__device__ __forceinline__ uint32_t check_fast(uint32_t& xa, uint32_t& xb, uint32_t& rp, uint32_t tbase, uint32_t lba,
+                                               uint32_t lbb, uint32_t ltm) {
   uint32_t out;
-  asm volatile(
-      "{\n"
-      " .reg .u32 sa, sb, aa, ab, ea, eb, qa, qb, fa, fb, ba, bb, w0, w1, va, vb, ca, cb, oa, ob, t, ada, adb, wa, wb;\n"
-      " .reg .pred pa, pb;\n"
-      // step 1: slot -> replicated entry -> x' = freq * (x >> 8) + bias
-      " and.b32 sa, %0, 255;\n and.b32 sb, %1, 255;\n"
-      " mad.lo.u32 aa, sa, 128, %4;\n mad.lo.u32 ab, sb, 128, %5;\n"
-      " ld.shared.u32 ea, [aa];\n ld.shared.u32 eb, [ab];\n"
-      " shr.u32 qa, %0, 8;\n shr.u32 qb, %1, 8;\n"
-      " shr.u32 fa, ea, 16;\n shr.u32 fb, eb, 16;\n"
-      " and.b32 ba, ea, 255;\n and.b32 bb, eb, 255;\n"
-      " mad.lo.u32 %0, fa, qa, ba;\n mad.lo.u32 %1, fb, qb, bb;\n"
-      " prmt.b32 w0, ea, eb, 0x0051;\n"
-      // step 2
-      " and.b32 sa, %0, 255;\n and.b32 sb, %1, 255;\n"
-      " mad.lo.u32 aa, sa, 128, %4;\n mad.lo.u32 ab, sb, 128, %5;\n"
-      " ld.shared.u32 ea, [aa];\n ld.shared.u32 eb, [ab];\n"
-      " shr.u32 qa, %0, 8;\n shr.u32 qb, %1, 8;\n"
-      " shr.u32 fa, ea, 16;\n shr.u32 fb, eb, 16;\n"
-      " and.b32 ba, ea, 255;\n and.b32 bb, eb, 255;\n"
-      " mad.lo.u32 %0, fa, qa, ba;\n mad.lo.u32 %1, fb, qb, bb;\n"
-      " prmt.b32 w1, ea, eb, 0x5100;\n"
-      " prmt.b32 %2, w0, w1, 0x7610;\n"
-      // renormalisation: ballot, prefix counts, one 16-bit word per low state
-      " setp.lt.u32 pa, %0, 65536;\n setp.lt.u32 pb, %1, 65536;\n"
-      " vote.sync.ballot.b32 va, pa, 0xffffffff;\n vote.sync.ballot.b32 vb, pb, 0xffffffff;\n"
-      " popc.b32 ca, va;\n popc.b32 cb, vb;\n"
-      " and.b32 t, va, %6;\n popc.b32 oa, t;\n"
-      " and.b32 t, vb, %6;\n popc.b32 ob, t;\n add.u32 ob, ob, ca;\n"
-      " mad.lo.u32 ada, oa, 2, %3;\n mad.lo.u32 adb, ob, 2, %3;\n"
-      " @pa ld.shared.u16 wa, [ada];\n @pb ld.shared.u16 wb, [adb];\n"
-      " @pa prmt.b32 %0, wa, %0, 0x5410;\n @pb prmt.b32 %1, wb, %1, 0x5410;\n"
-      " add.u32 t, ca, cb;\n mad.lo.u32 %3, t, 2, %3;\n"
-      "}\n"
-      : "+r"(xa), "+r"(xb), "=r"(out), "+r"(rp)
-      : "r"(tb0), "r"(tb1), "r"(ltm));
+  if (FIXED_BASE)
+    asm volatile(WS_CHECK_FAST_PTX("") : "+r"(xa), "+r"(xb), "=r"(out), "+r"(rp)
+                 : "r"(tbase), "r"(lba), "r"(lbb), "r"(ltm), "n"(kFixedTableBase));
+  else
+    asm volatile(WS_CHECK_FAST_PTX(WS_ADD_BASE_F) : "+r"(xa), "+r"(xb), "=r"(out), "+r"(rp)
+                 : "r"(tbase), "r"(lba), "r"(lbb), "r"(ltm), "n"(0));
   return out;
 }
 
 // Dictionary-block check in hand-written PTX: two decode steps in which state
 // A decodes the lane's even word and state B the following odd word (one
-// table, entry = word | bias << 16 | freq << 24), then one renormalisation
-// check. out0/out1 receive words (2s, 2s+1) of steps s = 0, 1 as lo | hi << 16.
-__device__ __forceinline__ void check_dict(uint32_t& xa, uint32_t& xb, uint32_t& rp, uint32_t tb, uint32_t ltm,
-                                           uint32_t& out0, uint32_t& out1) {
-  asm volatile(
-      "{\n"
-      " .reg .u32 sa, sb, aa, ab, ea, eb, qa, qb, fa, fb, ba, bb, va, vb, ca, cb, oa, ob, t, ada, adb, wa, wb;\n"
-      " .reg .pred pa, pb;\n"
-      " and.b32 sa, %0, 255;\n and.b32 sb, %1, 255;\n"
-      " mad.lo.u32 aa, sa, 128, %5;\n mad.lo.u32 ab, sb, 128, %5;\n"
-      " ld.shared.u32 ea, [aa];\n ld.shared.u32 eb, [ab];\n"
-      " shr.u32 qa, %0, 8;\n shr.u32 qb, %1, 8;\n"
-      " shr.u32 fa, ea, 24;\n shr.u32 fb, eb, 24;\n"
-      " prmt.b32 ba, ea, 0, 0x4442;\n prmt.b32 bb, eb, 0, 0x4442;\n"
-      " mad.lo.u32 %0, fa, qa, ba;\n mad.lo.u32 %1, fb, qb, bb;\n"
-      " prmt.b32 %2, ea, eb, 0x5410;\n"
-      " and.b32 sa, %0, 255;\n and.b32 sb, %1, 255;\n"
-      " mad.lo.u32 aa, sa, 128, %5;\n mad.lo.u32 ab, sb, 128, %5;\n"
-      " ld.shared.u32 ea, [aa];\n ld.shared.u32 eb, [ab];\n"
-      " shr.u32 qa, %0, 8;\n shr.u32 qb, %1, 8;\n"
-      " shr.u32 fa, ea, 24;\n shr.u32 fb, eb, 24;\n"
-      " prmt.b32 ba, ea, 0, 0x4442;\n prmt.b32 bb, eb, 0, 0x4442;\n"
-      " mad.lo.u32 %0, fa, qa, ba;\n mad.lo.u32 %1, fb, qb, bb;\n"
-      " prmt.b32 %3, ea, eb, 0x5410;\n"
-      " setp.lt.u32 pa, %0, 65536;\n setp.lt.u32 pb, %1, 65536;\n"
-      " vote.sync.ballot.b32 va, pa, 0xffffffff;\n vote.sync.ballot.b32 vb, pb, 0xffffffff;\n"
-      " popc.b32 ca, va;\n popc.b32 cb, vb;\n"
-      " and.b32 t, va, %6;\n popc.b32 oa, t;\n"
-      " and.b32 t, vb, %6;\n popc.b32 ob, t;\n add.u32 ob, ob, ca;\n"
-      " mad.lo.u32 ada, oa, 2, %4;\n mad.lo.u32 adb, ob, 2, %4;\n"
-      " @pa ld.shared.u16 wa, [ada];\n @pb ld.shared.u16 wb, [adb];\n"
-      " @pa prmt.b32 %0, wa, %0, 0x5410;\n @pb prmt.b32 %1, wb, %1, 0x5410;\n"
-      " add.u32 t, ca, cb;\n mad.lo.u32 %4, t, 2, %4;\n"
-      "}\n"
-      : "+r"(xa), "+r"(xb), "=r"(out0), "=r"(out1), "+r"(rp)
-      : "r"(tb), "r"(ltm));
+// table, entry = word | bias << 16 | freq << 24, at the lane's plane-0 row
+// offset lba), then one renormalisation check. out0/out1 receive words
+// (2s, 2s+1) of steps s = 0, 1 as lo | hi << 16.
+#define WS_CHECK_DICT_PTX(ADD)                                                             \
+  "{\n"                                                                                    \
+  " .reg .u32 aa, ab, ea, eb, qa, qb, fa, fb, ba, bb, va, vb, ca, cb, oa, ob, t, rb, ada, adb, wa, wb;\n" \
+  " .reg .pred pa, pb;\n"                                                                  \
+  WS_ROW_ADDR_D(ADD)                                                                       \
+  WS_LD_ENTRIES                                                                            \
+  " shr.u32 qa, %0, 8;\n shr.u32 qb, %1, 8;\n"                                            \
+  " shr.u32 fa, ea, 24;\n shr.u32 fb, eb, 24;\n"                                          \
+  " prmt.b32 ba, ea, 0, 0x4442;\n prmt.b32 bb, eb, 0, 0x4442;\n"                          \
+  " mad.lo.u32 %0, fa, qa, ba;\n mad.lo.u32 %1, fb, qb, bb;\n"                            \
+  " prmt.b32 %2, ea, eb, 0x5410;\n"                                                        \
+  WS_ROW_ADDR_D(ADD)                                                                       \
+  WS_LD_ENTRIES                                                                            \
+  " shr.u32 qa, %0, 8;\n shr.u32 qb, %1, 8;\n"                                            \
+  " shr.u32 fa, ea, 24;\n shr.u32 fb, eb, 24;\n"                                          \
+  " prmt.b32 ba, ea, 0, 0x4442;\n prmt.b32 bb, eb, 0, 0x4442;\n"                          \
+  " mad.lo.u32 %0, fa, qa, ba;\n mad.lo.u32 %1, fb, qb, bb;\n"                            \
+  " prmt.b32 %3, ea, eb, 0x5410;\n"                                                        \
+  WS_RENORM_PTX("%0", "%1", "%4", "%7")                                                     \
+  "}\n"
+
+template <bool FIXED_BASE>
+__device__ __forceinline__ void check_dict(uint32_t& xa, uint32_t& xb, uint32_t& rp, uint32_t tbase, uint32_t lba,
+                                           uint32_t ltm, uint32_t& out0, uint32_t& out1) {
+  if (FIXED_BASE)
+    asm volatile(WS_CHECK_DICT_PTX("") : "+r"(xa), "+r"(xb), "=r"(out0), "=r"(out1), "+r"(rp)
+                 : "r"(tbase), "r"(lba), "r"(ltm), "n"(kFixedTableBase));
+  else
+    asm volatile(WS_CHECK_DICT_PTX(WS_ADD_BASE_D) : "+r"(xa), "+r"(xb), "=r"(out0), "=r"(out1), "+r"(rp)
+                 : "r"(tbase), "r"(lba), "r"(ltm), "n"(0));
 }
 
 // Generic-path dictionary step: state A decodes word j, state B word j + 1.
 #define WS_DICT_STEP_C(ea, eb, va, vb)                                  \
   {                                                                     \
     if (va) {                                                           \
-      ea = lds32(tb0 + ((xa & 255u) << 7));                             \
+      ea = lds32(tb0 + ((xa & 255u) << 8));                             \
       xa = (ea >> 24) * (xa >> 8) + ((ea >> 16) & 255u);                \
     }                                                                   \
     if (vb) {                                                           \
-      eb = lds32(tb0 + ((xb & 255u) << 7));                             \
+      eb = lds32(tb0 + ((xb & 255u) << 8));                             \
       xb = (eb >> 24) * (xb >> 8) + ((eb >> 16) & 255u);                \
     }                                                                   \
   }
@@ -409,10 +439,9 @@ struct EscapeCursor {
   }
 };
 
-template <bool U16, bool REVERSE, bool DICT>
-__device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t* __restrict__ src,
-                          const uint32_t* __restrict__ tbl0, const uint32_t* __restrict__ tbl1, uint8_t* ring,
-                          uint32_t bar_base, uint32_t lane, ws_device_result* res) {
+template <bool U16, bool REVERSE, bool DICT, bool FIXED_BASE>
+__device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t* __restrict__ src, uint32_t tbase,
+                          uint8_t* ring, uint32_t bar_base, uint32_t lane, ws_device_result* res) {
   uint8_t* dst = reinterpret_cast<uint8_t*>(bd.dst);
   const uint32_t n = bd.nbytes;
   const uint32_t W = n / 2;
@@ -425,7 +454,8 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
   const uint32_t total_halves = (staged + WS_RING_HALF_BYTES - 1) / WS_RING_HALF_BYTES;
   const uint32_t ring_s = smem_addr(ring);
   const uint32_t ltm = lanemask_lt();
-  const uint32_t tb0 = smem_addr(tbl0) + lane * 4u, tb1 = smem_addr(tbl1) + lane * 4u;
+  const uint32_t lba = lane * 4u, lbb = lane * 4u + kRowBytes / 2;  // row offsets of planes 0 and 1
+  const uint32_t tb0 = tbase + lba, tb1 = tbase + lbb;
 
   // Half k of the payload goes to ring slot k & 1; even halves also refresh the
   // mirror behind the ring end. Both copies complete on the slot's mbarrier.
@@ -479,70 +509,84 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
   // bookkeeping runs only when the stream position reaches `next_event`.
   uint32_t g = 0;
   const uint32_t fast_groups = aligned ? W / WS_GROUP_WORDS : 0;
-  {
-    uint32_t next_event = 0;
-    uint4* p = reinterpret_cast<uint4*>(dst + lane * 16u);
-    // Dictionary blocks (HBM-bound): the destination vector of group g + 1 is
-    // loaded while group g decodes, and groups further ahead are pulled into L2
-    // by the TMA unit, so the DRAM latency of the destination stream stays
-    // hidden at high bandwidth. Byte-plane blocks are bound by instruction
-    // issue (two symbols per word): the four checks of a group hide the plain
-    // load's latency, and the look-ahead would cost ~29 instructions a group.
-    uint4 next_old = make_uint4(0, 0, 0, 0);
-    if (DICT) {
-      if (lane == 0)
-        for (uint32_t k = 1; k <= kPrefetchGroups && k < fast_groups; ++k)
-          prefetch_l2(dst + k * WS_GROUP_BYTES, WS_GROUP_BYTES);
-      if (fast_groups > 0) next_old = ldg128_early(p);
+  uint32_t next_event = 0;
+  auto at_event = [&]() {
+    stage();
+    const uint32_t recycle = issued < total_halves ? kHalfHalfwords * (issued - 1) : 0xFFFFFFFFu;
+    const uint32_t wait =
+        (ready < issued && bd.nwords > kHalfHalfwords * ready) ? kHalfHalfwords * ready - 255u : 0xFFFFFFFFu;
+    next_event = min(recycle, wait);
+    return ok;
+  };
+  // The lane's word pairs r0..r3 of group `grp` applied to the destination
+  // vector `old` (escaped words patched in first) and written back.
+  auto finish = [&](uint4* q, uint4 old, uint32_t grp, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+    if (DICT && esc.w < (grp + 1) * WS_GROUP_WORDS) esc.patch(grp, lane, r0, r1, r2, r3);
+    uint4 v;
+    if (U16) {
+      v.x = u16_apply(old.x, r0, REVERSE);
+      v.y = u16_apply(old.y, r1, REVERSE);
+      v.z = u16_apply(old.z, r2, REVERSE);
+      v.w = u16_apply(old.w, r3, REVERSE);
+    } else {
+      v.x = old.x ^ r0;
+      v.y = old.y ^ r1;
+      v.z = old.z ^ r2;
+      v.w = old.w ^ r3;
     }
+    *q = v;
+    ck.add(v.x, v.y, v.z, v.w);
+  };
+  uint4* p = reinterpret_cast<uint4*>(dst + lane * 16u);
+  if (DICT) {
+    // Dictionary blocks (HBM-bound at one symbol per word) run two groups per
+    // iteration: both destination vectors are loaded first, so ~200
+    // instructions of decode hide their latency, and lane 0 asks the TMA unit
+    // to pull the groups kPrefetchGroups ahead into L2. The per-iteration
+    // bookkeeping (ring events, stream position, prefetch) is paid once per
+    // 1 KiB; two groups read at most 256 stream words, which the staging
+    // guarantees at each event.
+    if (lane == 0 && fast_groups > 2) prefetch_l2(dst + 2 * WS_GROUP_BYTES, min(kPrefetchGroups, fast_groups - 2) * WS_GROUP_BYTES);
 #pragma unroll 1
-    for (; g < fast_groups; ++g, p += WS_GROUP_BYTES / 16) {
-      if (pos >= next_event) {
-        stage();
-        if (!ok) break;
-        const uint32_t recycle = issued < total_halves ? kHalfHalfwords * (issued - 1) : 0xFFFFFFFFu;
-        const uint32_t wait =
-            (ready < issued && bd.nwords > kHalfHalfwords * ready) ? kHalfHalfwords * ready - 255u : 0xFFFFFFFFu;
-        next_event = min(recycle, wait);
-      }
-      uint4 old;
-      if (DICT) {
-        old = next_old;
-        if (g + 1 < fast_groups) next_old = ldg128_early(p + WS_GROUP_BYTES / 16);
-        if (lane == 0 && g + 1 + kPrefetchGroups < fast_groups)
-          prefetch_l2(dst + (g + 1 + kPrefetchGroups) * WS_GROUP_BYTES, WS_GROUP_BYTES);
-      } else {
-        old = *p;
-      }
+    for (; g + 2 <= fast_groups; g += 2, p += 2 * WS_GROUP_BYTES / 16) {
+      if (pos >= next_event && !at_event()) break;
+      const uint4 old0 = ldg128_early(p);
+      const uint4 old1 = ldg128_early(p + WS_GROUP_BYTES / 16);
+      if (lane == 0 && g + 2 + kPrefetchGroups + 2 <= fast_groups)
+        prefetch_l2(dst + (g + 2 + kPrefetchGroups) * WS_GROUP_BYTES, 2 * WS_GROUP_BYTES);
       uint32_t rp = ring_s + (pos & (kRingHalfwords - 1)) * 2u;
       const uint32_t rp0 = rp;
       uint32_t r0, r1, r2, r3;
-      if (DICT) {
-        check_dict(xa, xb, rp, tb0, ltm, r0, r1);
-        check_dict(xa, xb, rp, tb0, ltm, r2, r3);
-      } else {
-        r0 = check_fast(xa, xb, rp, tb0, tb1, ltm);
-        r1 = check_fast(xa, xb, rp, tb0, tb1, ltm);
-        r2 = check_fast(xa, xb, rp, tb0, tb1, ltm);
-        r3 = check_fast(xa, xb, rp, tb0, tb1, ltm);
-      }
+      check_dict<FIXED_BASE>(xa, xb, rp, tbase, lba, ltm, r0, r1);
+      check_dict<FIXED_BASE>(xa, xb, rp, tbase, lba, ltm, r2, r3);
+      finish(p, old0, g, r0, r1, r2, r3);
+      check_dict<FIXED_BASE>(xa, xb, rp, tbase, lba, ltm, r0, r1);
+      check_dict<FIXED_BASE>(xa, xb, rp, tbase, lba, ltm, r2, r3);
+      finish(p + WS_GROUP_BYTES / 16, old1, g + 1, r0, r1, r2, r3);
       pos += (rp - rp0) >> 1;
-      if (DICT) esc.patch(g, lane, r0, r1, r2, r3);
-      uint4 v;
-      if (U16) {
-        v.x = u16_apply(old.x, r0, REVERSE);
-        v.y = u16_apply(old.y, r1, REVERSE);
-        v.z = u16_apply(old.z, r2, REVERSE);
-        v.w = u16_apply(old.w, r3, REVERSE);
-      } else {
-        v.x = old.x ^ r0;
-        v.y = old.y ^ r1;
-        v.z = old.z ^ r2;
-        v.w = old.w ^ r3;
-      }
-      *p = v;
-      ck.add(v.x, v.y, v.z, v.w);
     }
+  }
+  // Byte-plane blocks (bound by instruction issue at two symbols per word)
+  // run one group per iteration with a plain load: the group's four checks
+  // hide its latency. A dictionary block's odd last full group also runs here.
+#pragma unroll 1
+  for (; ok && g < fast_groups; ++g, p += WS_GROUP_BYTES / 16) {
+    if (pos >= next_event && !at_event()) break;
+    const uint4 old = DICT ? ldg128_early(p) : *p;
+    uint32_t rp = ring_s + (pos & (kRingHalfwords - 1)) * 2u;
+    const uint32_t rp0 = rp;
+    uint32_t r0, r1, r2, r3;
+    if (DICT) {
+      check_dict<FIXED_BASE>(xa, xb, rp, tbase, lba, ltm, r0, r1);
+      check_dict<FIXED_BASE>(xa, xb, rp, tbase, lba, ltm, r2, r3);
+    } else {
+      r0 = check_fast<FIXED_BASE>(xa, xb, rp, tbase, lba, lbb, ltm);
+      r1 = check_fast<FIXED_BASE>(xa, xb, rp, tbase, lba, lbb, ltm);
+      r2 = check_fast<FIXED_BASE>(xa, xb, rp, tbase, lba, lbb, ltm);
+      r3 = check_fast<FIXED_BASE>(xa, xb, rp, tbase, lba, lbb, ltm);
+    }
+    pos += (rp - rp0) >> 1;
+    finish(p, old, g, r0, r1, r2, r3);
   }
 
   // Generic path: the partial last group, the uncoded odd tail byte, and
@@ -612,6 +656,33 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
   ck.finish(lane, block, res);
 }
 
+// One block by its kind. FIXED_BASE: the table region starts at the shared
+// address kFixedTableBase, which the lookups then take as an immediate offset.
+template <bool REVERSE, bool FIXED_BASE>
+__device__ __forceinline__ void run_block(const ws_block_desc& bd, uint32_t block, const uint8_t* __restrict__ src,
+                                          uint32_t tbase, uint8_t* ring, uint32_t bar_base, uint32_t lane,
+                                          ws_device_result* res) {
+  switch (bd.kind) {
+    case WS_KIND_RAW:
+      raw_block(bd, block, src, lane, res);
+      break;
+    case WS_KIND_ANS_XOR:
+      ans_block<false, REVERSE, false, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
+      break;
+    case WS_KIND_ANS_U16:
+      ans_block<true, REVERSE, false, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
+      break;
+    case WS_KIND_DICT_XOR:
+      ans_block<false, REVERSE, true, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
+      break;
+    case WS_KIND_DICT_U16:
+      ans_block<true, REVERSE, true, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
+      break;
+    default:
+      if (lane == 0) report(res, WS_DEVERR_KIND, block);
+  }
+}
+
 // Bounds of the caller-owned arrays an allocation-free apply receives. The
 // plan-based apply builds its descriptors itself and runs unchecked.
 struct DescLimits {
@@ -658,7 +729,7 @@ __device__ __forceinline__ void apply_tile(const ws_tile_desc& tile, const ws_bl
     const uint32_t t = threadIdx.x;
     const uint32_t e = __ldg(tables + (uint64_t)tile.table * 512u + t);
     const uint4 v = make_uint4(e, e, e, e);
-    uint4* row = reinterpret_cast<uint4*>(tbl + (t >> 8) * kTableWords + (t & 255u) * 32u);
+    uint4* row = reinterpret_cast<uint4*>(tbl + (t & 255u) * (kRowBytes / 4) + (t >> 8) * 32u);
 #pragma unroll
     for (uint32_t k = 0; k < 8; ++k) row[(k + t) & 7u] = v;
   }
@@ -678,25 +749,11 @@ __device__ __forceinline__ void apply_tile(const ws_tile_desc& tile, const ws_bl
   }
   const uint8_t* src = payload + (bd.src - payload_offset);
   uint8_t* ring = smem + kRingOffset + warp * kRingStride;
-  switch (bd.kind) {
-    case WS_KIND_RAW:
-      raw_block(bd, block, src, lane, res);
-      break;
-    case WS_KIND_ANS_XOR:
-      ans_block<false, REVERSE, false>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
-      break;
-    case WS_KIND_ANS_U16:
-      ans_block<true, REVERSE, false>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
-      break;
-    case WS_KIND_DICT_XOR:
-      ans_block<false, REVERSE, true>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
-      break;
-    case WS_KIND_DICT_U16:
-      ans_block<true, REVERSE, true>(bd, block, src, tbl, tbl + kTableWords, ring, bar_base, lane, res);
-      break;
-    default:
-      if (lane == 0) report(res, WS_DEVERR_KIND, block);
-  }
+  const uint32_t tbase = smem_addr(tbl);
+  if (tbase == kFixedTableBase)
+    run_block<REVERSE, true>(bd, block, src, tbase, ring, bar_base, lane, res);
+  else
+    run_block<REVERSE, false>(bd, block, src, tbase, ring, bar_base, lane, res);
 }
 
 template <bool REVERSE>

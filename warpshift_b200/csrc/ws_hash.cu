@@ -38,6 +38,12 @@ struct HashTensor {
 
 __device__ __forceinline__ uint64_t term(uint64_t w, uint64_t i) { return ws_mix64(w ^ ((i + 1) * WS_TH_KPOS)); }
 
+// Asks the TMA unit to pull `bytes` (a multiple of 16, from a 16-byte-aligned
+// address) into L2 without waiting for them.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // Word i assembled from bytes (unaligned bases and the zero-padded tail).
 __device__ __forceinline__ uint64_t word_bytes(const uint8_t* p, uint64_t nbytes, uint64_t i) {
   uint64_t w = 0;
@@ -67,17 +73,37 @@ __global__ void __launch_bounds__(kHashThreads)
     uint64_t sum = 0;
     if (((uintptr_t)t.ptr & 15u) == 0) {
       // Lane l hashes words (w, w + 1) for w = w0 + 2l + 64k: 16-byte loads, 512
-      // contiguous bytes per warp and step, four steps in flight.
+      // contiguous bytes per warp and step. Software-pipelined: the next four
+      // steps' loads are in flight while the current four are hashed, and lane
+      // 0 has the TMA unit pull the steps after those into L2, so the warp never
+      // waits a full DRAM latency between batches.
       const uint4* v = reinterpret_cast<const uint4*>(t.ptr);
+      const uint64_t end = min(w1, full);
       uint64_t w = w0 + 2 * lane;
-      for (; w + 3 * 64 + 2 <= min(w1, full); w += 4 * 64) {
-        uint4 x[4];
+      if (w0 + 4 * 64 <= end) {
+        if (lane == 0 && w0 + 12 * 64 <= end) prefetch_l2(t.ptr + (w0 + 4 * 64) * 8, 8 * 64 * 8);
+        uint4 cur[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) x[k] = __ldg(v + (w + 64 * k) / 2);
+        for (int k = 0; k < 4; ++k) cur[k] = __ldg(v + (w + 64 * k) / 2);
+        uint64_t key = (w + 1) * WS_TH_KPOS;  // key of word w; the loop below advances it
+        for (; w + 3 * 64 + 2 <= end; w += 4 * 64) {
+          const bool more = w + 7 * 64 + 2 <= end;
+          uint4 nxt[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t i = w + 64 * k;
-          sum += term(((uint64_t)x[k].y << 32) | x[k].x, i) + term(((uint64_t)x[k].w << 32) | x[k].z, i + 1);
+          for (int k = 0; k < 4; ++k) nxt[k] = more ? __ldg(v + (w + 64 * (k + 4)) / 2) : make_uint4(0, 0, 0, 0);
+          const uint64_t ahead = (w - 2 * lane) + 12 * 64;  // first word of the batch after next
+          if (lane == 0 && ahead + 4 * 64 <= end) prefetch_l2(t.ptr + ahead * 8, 4 * 64 * 8);
+          // Position keys (i + 1) * KPOS of the lane's words i = w + 64k and i + 1
+          // by addition from the batch's first key: no 64-bit multiply per word.
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ka = key + (uint64_t)(64 * k) * WS_TH_KPOS;
+            sum += ws_mix64((((uint64_t)cur[k].y << 32) | cur[k].x) ^ ka) +
+                   ws_mix64((((uint64_t)cur[k].w << 32) | cur[k].z) ^ (ka + WS_TH_KPOS));
+          }
+          key += (uint64_t)(4 * 64) * WS_TH_KPOS;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) cur[k] = nxt[k];
         }
       }
       for (; w < w1; w += 64) {
