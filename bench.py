@@ -61,6 +61,8 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--scale", type=float, default=0.01, help="relative perturbation s of Teacher2")
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline time budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-reference-gpu", action="store_true",
+                   help="skip timing the reference's Triton restore kernel (baseline/_ref) on this GPU")
     p.add_argument("--ref-sample-gb", type=float, default=24.0,
                    help="reference arm: host bytes of the workload switched per step (its leading tensors)")
     p.add_argument("--threads", type=int, default=0, help="host encoder threads (0 = all)")
@@ -380,6 +382,117 @@ def verify_all_tensors(spec, gpu, state_is_b: bool, scale: float, device) -> int
     return len(spec.tensors)
 
 
+def reference_triton_restore(spec, gpu, state_is_b: bool, scale: float, policy: str, device, steps: int,
+                             warmup: int) -> dict:
+    """The reference's own Triton restore kernel (warpshift/delta.py:60-92, from the
+    reference package installed in baseline/_ref) timed on this GPU over the whole
+    workload, launched per batch as DeltaWeights.apply does (delta.py:300-324).
+
+    Its input is what the reference's nvCOMP decode would leave in the decoded
+    buffer (delta.py:313-316): per 16 MiB packet the XOR regrouped into byte planes
+    (mode 1), the zigzag planes (mode 3, U16 policy) or, below 16384 bytes, the raw
+    XOR (mode 0), all generated on the device from the Teachers. nvCOMP itself is
+    not installed anywhere here, so its decode time is not included: this is the
+    reference's switch minus its entropy decode. Returns the mean time of one
+    switch of the whole workload and checks that the weights end where they began.
+    """
+    import torch
+
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "warpshift" / "delta.py").exists():
+        return {"unavailable": "reference package not installed in baseline/_ref"}
+    if str(ref) not in sys.path:
+        sys.path.insert(0, str(ref))
+    from warpshift import delta as refdelta  # the reference's module: imports torch and triton only
+
+    from warpshift_b200 import synth
+
+    chunk, tile = refdelta._CHUNK_BYTES, refdelta._TILE_BYTES
+    packets, total = [], 0  # (mode, dst, num_bytes, arena offset)
+    for name, t in gpu.items():
+        n = t.numel() * t.element_size()
+        for off in range(0, n, chunk):
+            m = min(chunk, n - off)
+            if m < 16384:  # delta.py:185: smaller packets stay raw XOR
+                mode = 0
+            elif policy == "u16" and t.dtype == torch.bfloat16 and m % 2 == 0:
+                mode = 3
+            else:
+                mode = 1 if m % 2 == 0 else 2
+            packets.append((mode, t.data_ptr() + off, m, total, name, off))
+            total += (m + 255) // 256 * 256
+    free, _ = torch.cuda.mem_get_info(device)
+    if total + (2 << 30) > free:
+        return {"unavailable": f"the decoded residuals ({total / 1e9:.1f} GB) do not fit next to the workload"}
+    arena = torch.empty(total, dtype=torch.uint8, device=device)
+    for i, t in enumerate(spec.tensors):
+        a = synth.teacher1_tensor(t, i, device)
+        b = synth.perturb_(a.clone(), t, i, scale)
+        av, bv = a.reshape(-1).view(torch.uint8), b.reshape(-1).view(torch.uint8)
+        for mode, _, m, at, name, off in (p for p in packets if p[4] == t.name):
+            dst = arena[at : at + m]
+            x = torch.bitwise_xor(av[off : off + m], bv[off : off + m])
+            if mode == 1:  # delta.py:186
+                dst[: m // 2].copy_(x[0::2])
+                dst[m // 2 :].copy_(x[1::2])
+            elif mode == 3:  # delta.py:26-34 on the device
+                d = (bv[off : off + m].view(torch.int16).to(torch.int32) -
+                     av[off : off + m].view(torch.int16).to(torch.int32)) & 0xFFFF
+                d = torch.where(d >= 32768, d - 65536, d)
+                z = ((d << 1) ^ (d >> 15)) & 0xFFFF
+                dst[: m // 2].copy_(z & 0xFF)
+                dst[m // 2 :].copy_(z >> 8)
+            else:
+                dst.copy_(x)
+        del a, b
+    # Batches of at most 64 MiB of residuals, as _batch_layout bounds them (delta.py:37-57).
+    layout = refdelta._batch_layout([(m, m) for _, _, m, _, _, _ in packets])
+    launches = []
+    for batch in layout:
+        rows, tiles_of, base = [], [], None
+        for row, (index, _, _) in enumerate(batch["packets"]):
+            mode, dst, m, at, _, _ = packets[index]
+            base = at if base is None else base
+            rows.append((mode, dst, m, at - base, len(tiles_of)))
+            tiles_of.extend([row] * ((m + tile - 1) // tile))
+        launches.append((arena[base:], torch.tensor(rows, dtype=torch.int64, device=device),
+                         torch.tensor(tiles_of, dtype=torch.int32, device=device), len(tiles_of)))
+    stream = torch.cuda.current_stream(device)
+
+    def switch(reverse: bool) -> None:
+        for view, desc, tp, ntiles in launches:
+            refdelta._restore_batch[(ntiles,)](view, view, desc, tp, reverse, tile)
+
+    reverse = state_is_b
+    for _ in range(max(2, warmup + warmup % 2)):  # an even number: the weights end where they began
+        switch(reverse)
+        reverse = not reverse
+    n = steps + steps % 2
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(n):
+        switch(reverse)
+        reverse = not reverse
+    end.record(stream)
+    torch.cuda.synchronize(device)
+    ms = start.elapsed_time(end) / n
+    del arena, launches
+    torch.cuda.empty_cache()
+    verify_all_tensors(spec, gpu, state_is_b, scale, device)
+    traffic = 2 * spec.nbytes + total  # read + write weights, read the decoded residuals
+    return {
+        "ms_per_step": round(ms, 3),
+        "value": round(spec.nbytes / (ms * 1e-3) / 1e9, 2),
+        "unit": UNIT,
+        "launches_per_step": len(layout),
+        "algorithmic_bytes": traffic,
+        "achieved_gbs": round(traffic / (ms * 1e-3) / 1e9, 1),
+        "path": ("reference warpshift/delta.py _restore_batch (Triton) over decoded residuals generated on the device, "
+                 "one launch per 64 MiB batch; nvCOMP decode not installed, so not included"),
+        "modes": sorted({p[0] for p in packets}),
+    }
+
+
 # --------------------------------------------------------------------------- arms
 def run_reference(args) -> None:
     """Reference arm: the reference's switch on the host cores, rank 0 only."""
@@ -636,6 +749,13 @@ def run_ours(args) -> None:
         if tensor_hashes({t.name: ref})[t.name] != final_hashes[t.name]:
             raise RuntimeError(f"device hash of {t.name} differs from the regenerated teacher's")
     verified_total = int(sum_over_ranks(verified))
+    ref_gpu = None
+    if world == 1 and not args.no_reference_gpu:
+        try:
+            ref_gpu = reference_triton_restore(spec, gpu, state_is_b, args.scale, args.policy, device, args.steps,
+                                               args.warmup)
+        except Exception as exc:  # informative leg: report, never fail the bench
+            ref_gpu = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
     if rank != 0:
         return
     line = {
@@ -678,6 +798,7 @@ def run_ours(args) -> None:
             "kernel": "ws_apply_kernel (fused rANS decode + in-place apply)",
         },
         "verified_tensors": verified_total,
+        "reference_gpu_restore": ref_gpu,
         "full_copy": full_copy,
         "tensor_hash": {
             "ms": round(hash_ms, 3),

@@ -13,6 +13,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -129,6 +130,19 @@ int fail(int code, const std::string& msg) {
   return code;
 }
 
+// Device buffers for one device's tensor list and accumulators, allocated on
+// first use, grown when a call lists more tensors, and kept until exit, so a
+// call allocates nothing after the first. Calls on one device hold the mutex
+// for their whole duration (they end with a stream synchronisation).
+struct HashScratch {
+  std::mutex lock;
+  HashTensor* list = nullptr;
+  unsigned long long* acc = nullptr;
+  size_t capacity = 0;
+};
+constexpr int kHashMaxDevices = 64;
+HashScratch g_hash_scratch[kHashMaxDevices];
+
 }  // namespace
 
 static int ws_tensor_hashes_impl(const void* const* ptrs, const uint64_t* nbytes, uint64_t n, int device, void* stream,
@@ -147,30 +161,39 @@ static int ws_tensor_hashes_impl(const void* const* ptrs, const uint64_t* nbytes
   if (list.size() > 0xFFFFFFFFull) return fail(WS_ERR_INVALID, "too many tensors");
   std::vector<unsigned long long> acc(list.size(), 0);
   if (!list.empty()) {
+    if (device < 0 || device >= kHashMaxDevices) return fail(WS_ERR_INVALID, "bad device ordinal");
+    HashScratch& scratch = g_hash_scratch[device];
+    std::lock_guard<std::mutex> hold(scratch.lock);
     int prev = -1;
     cudaGetDevice(&prev);
     cudaError_t e = cudaSetDevice(device);
     cudaStream_t s = (cudaStream_t)stream;
-    HashTensor* d_list = nullptr;
-    unsigned long long* d_acc = nullptr;
     int sms = 0;
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-    if (e == cudaSuccess) e = cudaMallocAsync((void**)&d_list, list.size() * sizeof(HashTensor), s);
-    if (e == cudaSuccess) e = cudaMallocAsync((void**)&d_acc, acc.size() * sizeof(unsigned long long), s);
+    if (e == cudaSuccess && scratch.capacity < list.size()) {
+      cudaFree(scratch.list);
+      cudaFree(scratch.acc);
+      scratch.list = nullptr;
+      scratch.acc = nullptr;
+      scratch.capacity = 0;
+      const size_t cap = std::max<size_t>(list.size(), 1024);
+      e = cudaMalloc((void**)&scratch.list, cap * sizeof(HashTensor));
+      if (e == cudaSuccess) e = cudaMalloc((void**)&scratch.acc, cap * sizeof(unsigned long long));
+      if (e == cudaSuccess) scratch.capacity = cap;
+    }
     if (e == cudaSuccess)
-      e = cudaMemcpyAsync(d_list, list.data(), list.size() * sizeof(HashTensor), cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) e = cudaMemsetAsync(d_acc, 0, acc.size() * sizeof(unsigned long long), s);
+      e = cudaMemcpyAsync(scratch.list, list.data(), list.size() * sizeof(HashTensor), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(scratch.acc, 0, acc.size() * sizeof(unsigned long long), s);
     if (e == cudaSuccess) {
       const uint64_t warps_needed = nseg;
       const uint64_t blocks = std::min<uint64_t>((uint64_t)sms * kHashBlocksPerSm,
                                                  (warps_needed + kHashThreads / 32 - 1) / (kHashThreads / 32));
-      ws_tensor_hash_kernel<<<(unsigned)blocks, kHashThreads, 0, s>>>(d_list, (uint32_t)list.size(), nseg, d_acc);
+      ws_tensor_hash_kernel<<<(unsigned)blocks, kHashThreads, 0, s>>>(scratch.list, (uint32_t)list.size(), nseg,
+                                                                       scratch.acc);
       e = cudaGetLastError();
     }
     if (e == cudaSuccess)
-      e = cudaMemcpyAsync(acc.data(), d_acc, acc.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost, s);
-    if (d_list) cudaFreeAsync(d_list, s);
-    if (d_acc) cudaFreeAsync(d_acc, s);
+      e = cudaMemcpyAsync(acc.data(), scratch.acc, acc.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost, s);
     const cudaError_t es = cudaStreamSynchronize(s);
     if (e == cudaSuccess) e = es;
     if (prev >= 0) cudaSetDevice(prev);
