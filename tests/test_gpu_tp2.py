@@ -56,7 +56,10 @@ def _rank(rank: int, port: int, scenario: str, queue) -> None:
             x = synth.teacher1_tensor(t, i, device)
             cpu_base[t.name] = x.cpu()
             gpu[t.name] = synth.perturb_(x, t, i, 0.01)
-        delta = DeltaWeights(cpu_base, gpu, policy="auto")
+        # One encoder batch for the whole ~3 GB shard keeps the host arena in a
+        # single chunk, so the arena that plan_view exposes (and this test
+        # corrupts) is the one staged to the GPU, not a contiguous copy.
+        delta = DeltaWeights(cpu_base, gpu, policy="auto", encode_batch_bytes=4 << 30)
         teacher2 = {k: v.clone() for k, v in gpu.items()}
         spot = None
         if scenario == "corrupt" and rank == 1:
