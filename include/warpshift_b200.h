@@ -235,8 +235,9 @@ WS_API int ws_plan_load(const char* path, const ws_tensor_desc* tensors, uint64_
  * with one pass over the resident bytes on `device`. out[i] = 64-bit hash of the
  * nbytes[i] bytes at ptrs[i] (device memory, any alignment): with w_j the
  * little-endian 64-bit words (last one zero-padded),
- *   hash = mix64(sum_j mix64(w_j ^ (j + 1) * 0xC2B2AE3D27D4EB4F) + (nbytes + 1) * 0x165667B19E3779F9)
- * (arithmetic mod 2^64, mix64 = the splitmix64 finaliser). Keeps one small
+ *   hash = mix64(sum_j xmul(w_j ^ (j + 1) * 0xC2B2AE3D27D4EB4F) + (nbytes + 1) * 0x165667B19E3779F9)
+ * with xmul(x) = y ^ (y >> 32), y = x * 0x9E3779B97F4A7C15 (arithmetic mod 2^64,
+ * mix64 = the splitmix64 finaliser). Keeps one small
  * device buffer per device for the tensor list (allocated on the first call,
  * grown when a call lists more tensors, held until exit); calls on one device
  * are serialised; returns after `stream` completes. */

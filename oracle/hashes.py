@@ -8,11 +8,14 @@ this project's own definition, so there is no reference output to pin it to;
 Python loop and the GPU tests check the kernel against it.
 
     w_j  = little-endian 64-bit words of the bytes, the last one zero-padded
-    sum  = sum_j mix64(w_j ^ ((j + 1) * KPOS))        (mod 2^64)
+    sum  = sum_j xmul(w_j ^ ((j + 1) * KPOS))         (mod 2^64)
     hash = mix64(sum + (nbytes + 1) * KLEN)           (mod 2^64)
 
-mix64 is the splitmix64 finaliser (Steele, Lea and Flood, "Fast splittable
-pseudorandom number generators", OOPSLA 2014; constants as published).
+xmul(x) = y ^ (y >> 32) with y = x * KMUL (mod 2^64): one multiply by an odd
+constant and a fold of the high half into the low half, both bijections, per
+word. mix64, applied once per tensor, is the splitmix64 finaliser (Steele, Lea
+and Flood, "Fast splittable pseudorandom number generators", OOPSLA 2014;
+constants as published).
 """
 
 from __future__ import annotations
@@ -21,6 +24,7 @@ import numpy as np
 
 KPOS = 0xC2B2AE3D27D4EB4F
 KLEN = 0x165667B19E3779F9
+KMUL = 0x9E3779B97F4A7C15
 MASK = (1 << 64) - 1
 
 
@@ -33,12 +37,14 @@ def mix64_int(x: int) -> int:
     return x ^ (x >> 31)
 
 
-def _mix64(x: np.ndarray) -> np.ndarray:
-    x = x ^ (x >> np.uint64(30))
-    x = x * np.uint64(0xBF58476D1CE4E5B9)
-    x = x ^ (x >> np.uint64(27))
-    x = x * np.uint64(0x94D049BB133111EB)
-    return x ^ (x >> np.uint64(31))
+def xmul_int(x: int) -> int:
+    y = ((x & MASK) * KMUL) & MASK
+    return y ^ (y >> 32)
+
+
+def _xmul(x: np.ndarray) -> np.ndarray:
+    y = x * np.uint64(KMUL)
+    return y ^ (y >> np.uint64(32))
 
 
 def tensor_hash(data: bytes | np.ndarray) -> int:
@@ -52,7 +58,7 @@ def tensor_hash(data: bytes | np.ndarray) -> int:
         words = padded.view("<u8")
         pos = np.arange(1, words.size + 1, dtype=np.uint64) * np.uint64(KPOS)
         with np.errstate(over="ignore"):
-            terms = _mix64(words ^ pos)
+            terms = _xmul(words ^ pos)
         total = int(terms.sum(dtype=np.uint64))
     return mix64_int(total + (n + 1) * KLEN)
 
@@ -63,7 +69,7 @@ def tensor_hash_loop(data: bytes) -> int:
     total = 0
     for j in range(0, n, 8):
         w = int.from_bytes(data[j : j + 8].ljust(8, b"\0"), "little")
-        total += mix64_int(w ^ (((j // 8 + 1) * KPOS) & MASK))
+        total += xmul_int(w ^ (((j // 8 + 1) * KPOS) & MASK))
     return mix64_int(total + (n + 1) * KLEN)
 
 

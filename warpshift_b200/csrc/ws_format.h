@@ -126,6 +126,8 @@ typedef struct ws_device_result {
 // Per-tensor content hash (ws_tensor_hashes): word position and length keys.
 #define WS_TH_KPOS 0xC2B2AE3D27D4EB4Full
 #define WS_TH_KLEN 0x165667B19E3779F9ull
+#define WS_TH_KMUL 0x9E3779B97F4A7C15ull  // odd multiplier of the per-word mix
+
 
 #ifdef __CUDACC__
 #define WS_HD __host__ __device__ __forceinline__
@@ -146,4 +148,11 @@ WS_HD uint64_t ws_lane_hash(uint32_t a, uint32_t b, uint32_t lane) {
 }
 WS_HD uint64_t ws_block_hash(uint64_t lane_sum, uint64_t block_index) {
   return ws_mix64(lane_sum ^ ((block_index + 1) * WS_CK_K2));
+}
+// Per-word term of the tensor hash: xmul(x) = y ^ (y >> 32) with y = x * KMUL
+// (mod 2^64). Multiplying by an odd constant and folding the high half into the
+// low half are both bijections, so a change of one word always changes its term.
+WS_HD uint64_t ws_xmul64(uint64_t x) {
+  const uint64_t y = x * WS_TH_KMUL;
+  return y ^ (y >> 32);
 }

@@ -5,10 +5,12 @@
 // pass over the resident bytes. Definition (restated by the oracle): for a
 // tensor of N bytes, let w_i be its little-endian 64-bit words (the last one
 // zero-padded) and
-//   sum  = sum_i mix64(w_i ^ ((i + 1) * WS_TH_KPOS))   (mod 2^64)
+//   sum  = sum_i xmul(w_i ^ ((i + 1) * WS_TH_KPOS))    (mod 2^64)
 //   hash = mix64(sum + (N + 1) * WS_TH_KLEN)           (mod 2^64)
-// where mix64 is the splitmix64 finaliser. The terms are keyed by position and
-// summed, so any split of the words over warps gives the same value.
+// where xmul(x) = y ^ (y >> 32), y = x * WS_TH_KMUL (one 64-bit multiply and a
+// fold per word, ws_format.h) and mix64 is the splitmix64 finaliser applied once
+// per tensor. The terms are keyed by position and summed, so any split of the
+// words over warps gives the same value.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -37,7 +39,7 @@ struct HashTensor {
   uint64_t first_seg;  // first 64 KiB segment of this tensor in the flattened list
 };
 
-__device__ __forceinline__ uint64_t term(uint64_t w, uint64_t i) { return ws_mix64(w ^ ((i + 1) * WS_TH_KPOS)); }
+__device__ __forceinline__ uint64_t term(uint64_t w, uint64_t i) { return ws_xmul64(w ^ ((i + 1) * WS_TH_KPOS)); }
 
 // Asks the TMA unit to pull `bytes` (a multiple of 16, from a 16-byte-aligned
 // address) into L2 without waiting for them.
@@ -99,8 +101,8 @@ __global__ void __launch_bounds__(kHashThreads)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const uint64_t ka = key + (uint64_t)(64 * k) * WS_TH_KPOS;
-            sum += ws_mix64((((uint64_t)cur[k].y << 32) | cur[k].x) ^ ka) +
-                   ws_mix64((((uint64_t)cur[k].w << 32) | cur[k].z) ^ (ka + WS_TH_KPOS));
+            sum += ws_xmul64((((uint64_t)cur[k].y << 32) | cur[k].x) ^ ka) +
+                   ws_xmul64((((uint64_t)cur[k].w << 32) | cur[k].z) ^ (ka + WS_TH_KPOS));
           }
           key += (uint64_t)(4 * 64) * WS_TH_KPOS;
 #pragma unroll
