@@ -78,7 +78,7 @@ typedef struct ws_build_options {
 typedef struct ws_plan_stats {
   uint64_t runtime_bytes;      /* sum of tensor bytes (delta.py:122) */
   uint64_t skipped_bytes;      /* bytes of all-zero 16 MiB packets (delta.py:211) */
-  uint64_t zero_block_bytes;   /* bytes of all-zero 64 KiB blocks inside written packets */
+  uint64_t zero_block_bytes;   /* bytes of all-zero 128 KiB blocks inside written packets */
   uint64_t touched_bytes;      /* weight bytes the kernel reads and writes per apply */
   uint64_t payload_bytes;      /* sum of packet payload sizes (delta.py:124) */
   uint64_t arena_bytes;        /* bytes staged host->device per apply (delta.py:125) */

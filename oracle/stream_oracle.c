@@ -11,7 +11,7 @@
  * so only the residual and the applied bytes are compared with the reference
  * (delta.py:26-34, 74-92, 176-194), never the compressed bytes.
  *
- * Block layout (one 64 KiB weight block, payload 16-byte padded):
+ * Block layout (one weight block of at most 128 KiB, payload 16-byte padded):
  *   uint32 initial states[64]  (plane 0 lanes 0..31, then plane 1 lanes 0..31)
  *   uint16 renormalisation words in decode order
  * Word i (bytes 2i, 2i+1 of the block) belongs to lane (i % 256) / 8 and is
@@ -39,6 +39,7 @@
 #include <string.h>
 
 #define O_L 65536u
+#define O_BLOCK_WORDS 65536u /* 16-bit words of the largest block (128 KiB) */
 
 typedef struct {
   uint64_t dst;
@@ -151,7 +152,7 @@ static inline uint16_t o_unrotate(uint16_t y) { return (uint16_t)(y ^ ((y & 0x80
 
 /* Apply one block to dst (host memory). Returns 0 or O_ERR_*. */
 int wso_apply_block(const o_block* b, const uint8_t* payload, const uint32_t* table512, uint8_t* dst, int reverse,
-                    uint16_t* scratch_words /* >= 32768 */) {
+                    uint16_t* scratch_words /* >= O_BLOCK_WORDS */) {
   const uint32_t n = b->nbytes;
   if (b->kind == O_RAW) {
     if (b->clen < n) return O_ERR_BOUNDS;
@@ -249,7 +250,7 @@ typedef struct {
 
 static void* o_worker(void* arg) {
   o_job* j = (o_job*)arg;
-  static __thread uint16_t words[32768];
+  static __thread uint16_t words[O_BLOCK_WORDS];
   for (uint64_t t = (uint64_t)j->tid; t < j->ntiles; t += (uint64_t)j->nthreads) {
     const o_tile* tile = &j->tiles[t];
     const uint32_t* table = tile->table == 0xFFFFFFFFu ? 0 : j->tables + 512ull * tile->table;

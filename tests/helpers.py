@@ -9,6 +9,9 @@ import torch
 
 from oracle import stream as ostream
 from warpshift_b200 import _lib
+from warpshift_b200.delta import _BLOCK_BYTES
+
+BLOCK_WORDS = _BLOCK_BYTES // 2  # 16-bit words per rANS block
 
 
 def bf16_pair(numel: int, scale: float, seed: int) -> tuple[torch.Tensor, torch.Tensor]:
@@ -25,7 +28,7 @@ def edge_pair(seed: int = 0, scale: float = 0.01, big: bool = True) -> tuple[dic
     Tiny raw-XOR tensors (< 16384 B, delta.py:185), the 16383/16384 boundary,
     odd byte counts (mode 2, delta.py:186/189), fp32 and uint8 tensors (XOR only,
     delta.py:190), unchanged tensors (SKIP, delta.py:181), partial 512-byte groups
-    and 64 KiB blocks, and (with ``big``) a tensor spanning two 16 MiB packets.
+    and blocks, and (with ``big``) a tensor spanning two 16 MiB packets.
     """
     rng = np.random.default_rng(seed)
     a: dict[str, torch.Tensor] = {}
@@ -55,7 +58,7 @@ def edge_pair(seed: int = 0, scale: float = 0.01, big: bool = True) -> tuple[dic
 
 
 def _lane_positions(lane: int, count: int) -> np.ndarray:
-    """Word indexes of a 64 KiB block that decode lane ``lane`` owns: words
+    """Word indexes of a block that decode lane ``lane`` owns: words
     8*lane .. 8*lane+7 of every 256-word (512-byte) group, in stream order."""
     groups = np.arange((count + 7) // 8)[:, None] * 256
     return (groups + 8 * lane + np.arange(8)[None, :]).reshape(-1)[:count]
@@ -66,7 +69,7 @@ def adversarial_pair(seed: int = 0) -> tuple[dict[str, torch.Tensor], dict[str, 
 
     Every pattern is built twice: as an XOR residual (B = A ^ r) and as a U16
     residual (B = A + d mod 2^16), so that both transforms meet it exactly.
-    Patterns: a single changed word among three 64 KiB blocks, two distinct
+    Patterns: a single changed word among three blocks, two distinct
     words, exactly 255 and 256 distinct words (the dictionary limit), extreme
     skew (one word 99.9 %), rare words that fill one decode lane's escape list
     to its limit of 64 and past it, one residual word everywhere (a single
@@ -95,28 +98,28 @@ def adversarial_pair(seed: int = 0) -> tuple[dict[str, torch.Tensor], dict[str, 
         r[:size] = values  # every value at least once
         return r[rng.permutation(n)]
 
-    r = np.zeros(3 * 32768, np.uint32)
+    r = np.zeros(3 * BLOCK_WORDS, np.uint32)
     r[40000] = 0x0040
     put_words("one_word", r)
-    put_words("two_words", rng.integers(0, 2, 2 * 32768).astype(np.uint32))
-    put_words("distinct_255", alphabet(255, 2 * 32768 + 100))
-    put_words("distinct_256", alphabet(256, 2 * 32768 + 100))
-    r = np.where(rng.random(2 * 32768) < 0.999, 0, rng.integers(1, 4, 2 * 32768)).astype(np.uint32)
+    put_words("two_words", rng.integers(0, 2, 2 * BLOCK_WORDS).astype(np.uint32))
+    put_words("distinct_255", alphabet(255, 2 * BLOCK_WORDS + 100))
+    put_words("distinct_256", alphabet(256, 2 * BLOCK_WORDS + 100))
+    r = np.where(rng.random(2 * BLOCK_WORDS) < 0.999, 0, rng.integers(1, 4, 2 * BLOCK_WORDS)).astype(np.uint32)
     put_words("skew", r)
     for escapes in (64, 126):
         # 192 frequent words (the largest dictionary kept beside escapes) and
         # escapes / 2 rare words, each twice, all in lane 5 of the first block.
         frequent = rng.permutation(np.arange(1, 65536, dtype=np.uint32))[:192]
-        r = frequent[rng.integers(0, 192, 2 * 32768)]
+        r = frequent[rng.integers(0, 192, 2 * BLOCK_WORDS)]
         pool = np.setdiff1d(np.arange(1, 65536, dtype=np.uint32), frequent)
         r[_lane_positions(5, escapes)] = np.repeat(rng.choice(pool, escapes // 2, replace=False), 2)
         put_words(f"lane5_escapes_{escapes}", r)
     for word in (0x0101, 0x8000, 0xFFFF):  # one residual word everywhere: single-symbol tables
-        put_words(f"constant_{word:04x}", np.full(2 * 32768 + 50, word, np.uint32))
+        put_words(f"constant_{word:04x}", np.full(2 * BLOCK_WORDS + 50, word, np.uint32))
     steps = np.array([0, 0x8000, 0x7FFF, 0xFFFF, 1], np.uint32)
-    put_words("u16_extremes", steps[rng.integers(0, 5, 32768 + 4096)])
+    put_words("u16_extremes", steps[rng.integers(0, 5, BLOCK_WORDS + 4096)])
     put_words("packet_16mib", alphabet(40, (16 << 20) // 2))
-    u = rng.integers(0, 256, 3 * 65536 + 3, dtype=np.uint8)
+    u = rng.integers(0, 256, 3 * _BLOCK_BYTES + 3, dtype=np.uint8)
     v = u ^ np.array([0, 1, 2], np.uint8)[rng.integers(0, 3, u.size)]
     v[-1] = u[-1] ^ 0x80
     a["buffer:u8_odd_blocks"], b["buffer:u8_odd_blocks"] = torch.from_numpy(u), torch.from_numpy(v)

@@ -11,7 +11,7 @@ kernel and compares every tensor, byte for byte, with the regenerated Teacher
   column-parallel QKV and gate/up, row-parallel o/down, vocabulary-parallel
   embedding and lm_head);
 * the sparse Mixtral-8x7B TP=8 shard, whose skipped packets (delta.py:181-182,
-  209-212) and all-zero 64 KiB blocks must match the oracle's count.
+  209-212) and all-zero blocks must match the oracle's count.
 """
 
 from __future__ import annotations
@@ -24,7 +24,7 @@ import torch
 
 from oracle import semantics as sem
 from warpshift_b200 import synth
-from warpshift_b200.delta import DeltaWeights
+from warpshift_b200.delta import _BLOCK_BYTES, DeltaWeights
 
 pytestmark = pytest.mark.gpu
 
@@ -86,8 +86,8 @@ def test_config4_mixtral_tp8_sparse_skips_like_the_oracle(cuda_device) -> None:
     spec = synth.model_spec(dataclasses.replace(synth.MIXTRAL_8X7B, layers=2), tp=8, rank=3)
     cpu_base, gpu = generate(spec, cuda_device, 0.01)
     # Oracle count: packets of 16 MiB whose XOR is all zero are skipped
-    # (delta.py:181-182, 209-212); inside written packets, 64 KiB blocks whose
-    # XOR is all zero are omitted from the stream.
+    # (delta.py:181-182, 209-212); inside written packets, blocks whose XOR is
+    # all zero are omitted from the stream.
     skipped = zero_blocks = 0
     for name, target in gpu.items():
         a = cpu_base[name].reshape(-1).view(torch.uint8).numpy()
@@ -97,9 +97,9 @@ def test_config4_mixtral_tp8_sparse_skips_like_the_oracle(cuda_device) -> None:
             if not xor.any():
                 skipped += xor.size
                 continue
-            for k in range(0, xor.size, 65536):
-                if not xor[k : k + 65536].any():
-                    zero_blocks += xor[k : k + 65536].size
+            for k in range(0, xor.size, _BLOCK_BYTES):
+                if not xor[k : k + _BLOCK_BYTES].any():
+                    zero_blocks += xor[k : k + _BLOCK_BYTES].size
     assert skipped > 0.5 * spec.nbytes  # most of the shard is unchanged
     delta = DeltaWeights(cpu_base, gpu, policy="auto")
     assert delta.stats["skipped_bytes"] == skipped

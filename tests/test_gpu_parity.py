@@ -15,7 +15,7 @@ import torch
 from oracle import semantics as sem
 from tests.helpers import adversarial_pair, as_bytes, edge_pair
 from warpshift_b200 import synth
-from warpshift_b200.delta import DeltaWeights
+from warpshift_b200.delta import _BLOCK_BYTES, DeltaWeights
 
 pytestmark = pytest.mark.gpu
 
@@ -99,9 +99,9 @@ def test_decoded_residual_matches_oracle(cuda_device, policy: str, coding: str) 
             mode = delta.stats["mode_counts"]
             assert "U16_ANS" in mode
             ok = np.array_equal(got, d) or np.array_equal(got, xor)
-            if not ok:  # blocks may mix (per-block raw fallback): check per 64 KiB block
-                for off in range(0, got.size, 65536):
-                    sl = slice(off, off + 65536)
+            if not ok:  # blocks may mix (per-block raw fallback): check block by block
+                for off in range(0, got.size, _BLOCK_BYTES):
+                    sl = slice(off, off + _BLOCK_BYTES)
                     assert np.array_equal(got[sl], d[sl]) or np.array_equal(got[sl], xor[sl]), (name, off)
         else:
             np.testing.assert_array_equal(got, xor, err_msg=name)

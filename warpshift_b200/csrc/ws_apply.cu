@@ -3,7 +3,7 @@
 // Replaces, in one kernel, nvCOMP's batched ANS decode into a scratch buffer
 // (warpshift/delta.py:313-316) and the Triton read-modify-write kernel
 // _restore_batch (delta.py:60-92, launched at 317-324). The decoded residual
-// never touches HBM: per 64 KiB block the kernel reads the compressed payload
+// never touches HBM: per 128 KiB block the kernel reads the compressed payload
 // once and reads + writes the destination weights once.
 //
 // Work decomposition: one CTA (16 warps) per tile of up to 16 blocks of one
@@ -693,7 +693,7 @@ struct DescLimits {
 
 // A block descriptor the kernel can follow without leaving the payload: a
 // 16-byte-aligned payload range inside the caller's arena (cp.async.bulk needs
-// 16-byte alignment), 1..65536 weight bytes, a known kind, and a raw payload
+// 16-byte alignment), 1..WS_BLOCK_BYTES weight bytes, a known kind, and a raw payload
 // that holds every weight byte it XORs.
 __device__ __forceinline__ bool block_in_bounds(const ws_block_desc& bd, uint64_t payload_bytes) {
   return (bd.src & 15u) == 0 && (bd.clen & 15u) == 0 && bd.src <= payload_bytes &&

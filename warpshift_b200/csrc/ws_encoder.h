@@ -8,7 +8,7 @@
 
 namespace ws {
 
-// One encoded 64 KiB block of a packet.
+// One encoded block (WS_BLOCK_BYTES of weights) of a packet.
 struct EncodedBlock {
   uint32_t offset;  // byte offset of the block inside its packet
   uint32_t nbytes;  // weight bytes covered

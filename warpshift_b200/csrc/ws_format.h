@@ -10,7 +10,7 @@
 //     dst = dst +/- unzigzag(residual) modulo 2^16 (delta.py:74-92).
 // The entropy stage is this project's own chunked, interleaved rANS code,
 // which replaces nvCOMP's ANS (delta.py:111-113, 164-174, 313-316):
-//   * a packet is cut into blocks of 64 KiB of weight bytes; one warp decodes
+//   * a packet is cut into blocks of 128 KiB of weight bytes; one warp decodes
 //     one block; 32 lanes x 2 interleaved 32-bit states (plane 0 = low byte of
 //     each uint16 word, plane 1 = high byte) share one 16-bit renormalisation
 //     word stream;
@@ -30,7 +30,7 @@
 #include <stdint.h>
 
 #define WS_PACKET_BYTES (16u << 20)  // delta.py:20
-#define WS_BLOCK_BYTES 65536u        // rANS chunk; one warp per block
+#define WS_BLOCK_BYTES 131072u       // rANS chunk; one warp per block
 #define WS_COMPRESS_MIN 16384u       // delta.py:185 (compression tried only at >= 16384 B)
 #define WS_GROUP_WORDS 256u          // one 512-byte group per warp step of 8 words/lane
 #define WS_GROUP_BYTES 512u
@@ -48,7 +48,7 @@
 // Packet modes (delta.py:23 _MODES) plus SKIP.
 enum ws_mode { WS_MODE_XOR_RAW = 0, WS_MODE_XOR_GROUP2_ANS = 1, WS_MODE_XOR_ANS = 2, WS_MODE_U16_ANS = 3, WS_MODE_SKIP = 4 };
 
-// Block kinds (per 64 KiB block inside a packet). All-zero blocks are omitted.
+// Block kinds (per 128 KiB block inside a packet). All-zero blocks are omitted.
 enum ws_kind {
   WS_KIND_RAW = 0,       // payload = raw XOR bytes
   WS_KIND_ANS_XOR = 1,   // byte planes, XOR apply
@@ -81,7 +81,7 @@ enum ws_kind {
 typedef struct ws_block_desc {
   uint64_t dst;      // absolute address of the block's first weight byte
   uint64_t src;      // byte offset of the block payload inside the plan arena
-  uint32_t nbytes;   // weight bytes covered (1 .. 65536)
+  uint32_t nbytes;   // weight bytes covered (1 .. WS_BLOCK_BYTES)
   uint32_t clen;     // payload bytes (multiple of 16)
   uint32_t nwords;   // ANS: stream halfwords incl. the 128-halfword state header; RAW: 0
   uint16_t kind;     // ws_kind

@@ -3,7 +3,7 @@
 //
 // Per batch of packets:
 //   1. the base (A) bytes are copied host -> device;
-//   2. stats_kernel: per 64 KiB block, zero detection, byte-plane histograms and
+//   2. stats_kernel: per 128 KiB block, zero detection, byte-plane histograms and
 //      distinct-word tables of both residual transforms, checksum lane sums of
 //      A and B, odd tail byte;
 //   3. the host builds each packet's tables with the same code as the host
@@ -41,7 +41,7 @@ constexpr uint32_t kStatsThreads = 256;
 constexpr uint32_t kLocalSlots = 512;     // per-CTA distinct-word table
 constexpr uint32_t kPacketSlots = 1024;   // per-packet distinct-word table
 constexpr uint32_t kEncWarps = 8;         // blocks per encode CTA
-constexpr uint32_t kOutHalfwords = WS_HEADER_HALFWORDS + 32768u;  // header + worst-case stream
+constexpr uint32_t kOutHalfwords = WS_HEADER_HALFWORDS + WS_BLOCK_BYTES / 2;  // header + worst-case stream
 constexpr uint32_t kMaxDistinct = 255;
 
 struct PacketStats {  // device, one per packet of the batch
@@ -58,7 +58,7 @@ struct BlockStats {  // device, one per block of the batch
   unsigned long long lane_sum[2];  // [0] target (B) bytes, [1] base (A) bytes
 };
 
-struct BlockJob {  // one 64 KiB block of the batch
+struct BlockJob {  // one block (WS_BLOCK_BYTES) of the batch
   const uint8_t* base;    // device copy of A
   const uint8_t* target;  // resident B
   uint32_t nbytes;
@@ -604,7 +604,7 @@ class Uploader {
   std::vector<Worker> workers_;
 };
 
-// The device work of one batch: its packets, 64 KiB block jobs and A uploads.
+// The device work of one batch: its packets, block jobs and A uploads.
 struct BatchInput {
   size_t first = 0, last = 0;
   std::vector<BlockJob> blocks;

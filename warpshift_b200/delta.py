@@ -28,7 +28,7 @@ from . import _lib
 
 _CHUNK_BYTES = 16 * 1024**2  # delta.py:20, packet size
 _BATCH_BYTES = 64 * 1024**2  # delta.py:21, default bound of _batch_layout
-_BLOCK_BYTES = 65536  # rANS block: one warp decodes one block
+_BLOCK_BYTES = 131072  # rANS block: one warp decodes one block (WS_BLOCK_BYTES)
 _STAGING_BATCH_BYTES = 64 * 1024**2  # H2D staging batch bound, as the reference's BATCH_BYTES (delta.py:21)
 # A packet whose 16-bit residual words take <= 255 values may be coded one
 # symbol per word (half the decode work of the two byte planes); it is chosen
