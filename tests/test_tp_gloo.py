@@ -67,11 +67,13 @@ def _rank_main(rank: int, world: int, port: int, scenario: str, queue) -> None:
             def apply(self, *, reverse):
                 if scenario == "apply_error" and rank == 1:
                     raise RuntimeError("delta decode failed: device errors 0x1")
+                if scenario == "undo_error" and rank == 0 and not reverse:
+                    raise RuntimeError("copy engine error")  # rank 0's switch back fails
                 src = self.base if reverse else self.target
                 with torch.no_grad():
                     for n, t in self.tensors.items():
                         t.copy_(src[n])
-                bad = scenario == "checksum_mismatch" and rank == 1
+                bad = scenario in ("checksum_mismatch", "undo_error") and rank == 1
                 self.last_apply = {"ok": True, "checksum": 1000 + rank + (7 if bad else 0), "expected": 1000 + rank}
 
             confirm = DeltaWeights.confirm
@@ -123,7 +125,7 @@ def _run(scenario: str) -> dict[int, tuple]:
     return results
 
 
-@pytest.mark.parametrize("scenario", ["success", "apply_error", "checksum_mismatch", "stale_source"])
+@pytest.mark.parametrize("scenario", ["success", "apply_error", "checksum_mismatch", "stale_source", "undo_error"])
 def test_two_ranks_agree_before_writing_and_confirm_after(scenario: str) -> None:
     results = _run(scenario)
     for rank, (outcome, current, weight) in results.items():
@@ -133,6 +135,11 @@ def test_two_ranks_agree_before_writing_and_confirm_after(scenario: str) -> None
         elif scenario == "stale_source":
             assert "rank 1" in outcome and "source model" in outcome
             assert current == "b" and weight == 2.0 + rank  # no rank wrote
+        elif scenario == "undo_error":
+            # rank 1 missed its checksum; rank 0 switched but could not switch back,
+            # and every rank's error names that.
+            assert "rank 1" in outcome and "switching back to b failed" in outcome
+            assert current == "b"
         else:
             assert outcome.startswith("error") and "rank 1" in outcome
             assert current == "b"  # identity not committed on any rank

@@ -230,8 +230,10 @@ def _confirm_switch(model: torch.nn.Module, command: dict[str, Any], device_grou
             undo = dict(command, model=command["from_model"])
             try:
                 _restore(model, undo)
-            except Exception as undo_exc:  # leave the first error in place; log the undo failure
+            except Exception as undo_exc:  # this rank's weights are then neither model: say so
                 _log.error("Switching back to %s failed: %s", command["from_model"], undo_exc)
+                outcome.error += (f"; switching back to {command['from_model']} failed "
+                                  f"({type(undo_exc).__name__}: {undo_exc})")
 
 
 def model_weight_loader(model: torch.nn.Module, named_tensors: Iterable[tuple[str, torch.Tensor]]) -> None:
