@@ -57,6 +57,9 @@ def parse_args() -> argparse.Namespace:
                    help="default: llama3-8b on one GPU, llama3-70b at TP = number of GPUs otherwise")
     p.add_argument("--escapes", type=int, default=0,
                    help="word dictionaries with escape lists: 0 when smaller (default), -1 never, 1 whenever eligible")
+    p.add_argument("--split", type=int, default=0,
+                   help="split-word dictionaries (low k bits stored raw): 0 the k estimated smallest (default), "
+                        "-1 never, 1 / 2 / 4 that k whenever eligible")
     p.add_argument("--policy", default="xor", choices=["auto", "xor", "u16"])
     p.add_argument("--scale", type=float, default=0.01, help="relative perturbation s of Teacher2")
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline time budget")
@@ -179,7 +182,7 @@ def workload_spec(args, world: int, rank: int):
 
 def workload_config(args, desc: str, nbytes: int) -> dict:
     """The workload's identity: the same object in both arms' lines."""
-    return {"workload": desc, "policy": args.policy, "scale": args.scale, "escapes": args.escapes,
+    return {"workload": desc, "policy": args.policy, "scale": args.scale, "escapes": args.escapes, "split": args.split,
             "l2": f"inputs ({nbytes / 1e9:.2f} GB of weights per rank) larger than the 126 MB L2; no flush"}
 
 
@@ -569,7 +572,8 @@ def run_ours(args) -> None:
             if rank == 0 and world == 1 and not args.no_cpu_baseline:
                 cpu_base_line = reference_cpu_baseline(spec, cpu_base, gpu, args.policy, args.cpu_seconds)
             t0 = time.perf_counter()
-            delta = DeltaWeights(cpu_base, gpu, policy=args.policy, threads=args.threads, escapes=args.escapes)
+            delta = DeltaWeights(cpu_base, gpu, policy=args.policy, threads=args.threads, escapes=args.escapes,
+                                 split=args.split)
             prepare_s = time.perf_counter() - t0
             del cpu_base
         if group is not None:
@@ -601,6 +605,15 @@ def run_ours(args) -> None:
         t = torch.tensor([x], dtype=torch.float64, device=device)
         dist.all_reduce(t, group=group)
         return float(t.item())
+
+    def per_rank(values: list[float]) -> list[list[float]]:
+        """Every rank's `values`, in rank order (one all-gather)."""
+        mine = torch.tensor(values, dtype=torch.float64, device=device)
+        if group is None:
+            return [mine.tolist()]
+        everyone = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(everyone, mine, group=group)
+        return [t.tolist() for t in everyone]
 
     props = torch.cuda.get_device_properties(device)
     gpu_id = f"GPU-{props.uuid}" if getattr(props, "uuid", None) else str(local)
@@ -725,6 +738,8 @@ def run_ours(args) -> None:
     # Per-rank fraction of its own roofline; the minimum over ranks is reported.
     min_rank_frac = -max_over_ranks(-(rank_roof_ms / rank_e2e_ms)) if rank_e2e_ms else None
     h2d_slowest = -max_over_ranks(-h2d_gbs) if h2d_gbs == h2d_gbs else h2d_gbs
+    ranks_h2d_e2e_kernel = per_rank([h2d_gbs, rank_e2e_ms if rank_e2e_ms else float("nan"),
+                                     kernel_ms / args.steps])
     # On-device per-tensor hashes of the switched weights (the replacement for the
     # acceptance check's D2H sha256), timed over every tensor of this rank.
     from warpshift_b200.verify import tensor_hashes
@@ -822,6 +837,8 @@ def run_ours(args) -> None:
             "kernel_step_ms": [round(x, 3) for x in step_ms],
             "kernel_median_ms": per_direction(step_ms, k_reverse),
             "e2e_step_ms": [round(x, 3) for x in e_step_ms],
+            "per_rank": [{"h2d_gbs": None if h != h else round(h, 2), "e2e_ms": None if e != e else round(e, 3),
+                          "kernel_ms": round(k, 3)} for h, e, k in ranks_h2d_e2e_kernel],
         },
     }
     if cpu_base_line is not None:

@@ -73,6 +73,9 @@ typedef struct ws_build_options {
   int32_t host_fallback;    /* 1: when the GPU encoder cannot get its device buffers even with 32 MiB
                                batches, encode on host threads instead; 0 (default): fail with
                                WS_ERR_NOMEM */
+  int32_t split;            /* split-word dictionaries (the low k = 1, 2 or 4 bits of every word
+                               stored raw, the rest coded): 0 (default) the k estimated smallest,
+                               k = 0 included; < 0 never; 1, 2 or 4: that k whenever eligible */
 } ws_build_options;
 
 typedef struct ws_plan_stats {
@@ -203,7 +206,9 @@ WS_API int ws_plan_get_view(const ws_plan* plan, ws_plan_view* out);
  * WS_NOALLOC_MAX_TILES + 1 slots (256 KiB) inside the library, held by every
  * GPU that loads the library until exit; more than WS_NOALLOC_MAX_TILES tiles
  * per call is rejected with WS_ERR_INVALID. The first call on a device looks up
- * that array's device address (module set-up). All calls on a device share the
+ * that array's device address and loads the entry point's kernels for both
+ * directions (module set-up), so later calls allocate nothing, whatever
+ * their direction. All calls on a device share the
  * array: calls that overlap on the GPU race and must be serialised by the
  * caller. The call is synchronous: it reads its result back to the host and
  * returns after `stream` completes, so it cannot be made while `stream` is

@@ -33,6 +33,15 @@
  * entries grouped by lane: word index (bits 0-15) | residual word (16-31). The
  * listed words' residuals are the listed values (their stream symbol decodes
  * as 0); an entry outside the block or not owned by its lane is an error.
+ *
+ * Dictionary blocks whose flag bits 2-3 hold c != 0 split every word: its low
+ * k = 1, 2, 4 (c = 1, 2, 3) bits are not in the stream but in a raw section at
+ * byte (2 * nwords + 15) & ~15 (escape lists, if any, move behind it). With
+ * G = 4 / k groups per uint32, group g's bits for lane l are in uint32
+ * (g / G) * 32 + l, starting at bit (g % G) * 4k; the lane's word j sits at
+ * bit (j odd ? 16 : 0) + (j / 2) * k from there. The section has
+ * ceil(ceil(W / 256) / G) * 128 bytes. The residual word is the decoded (or
+ * listed) word ORed with its raw bits.
  */
 #include <pthread.h>
 #include <stdint.h>
@@ -152,7 +161,8 @@ static inline uint16_t o_unrotate(uint16_t y) { return (uint16_t)(y ^ ((y & 0x80
 
 /* Apply one block to dst (host memory). Returns 0 or O_ERR_*. */
 int wso_apply_block(const o_block* b, const uint8_t* payload, const uint32_t* table512, uint8_t* dst, int reverse,
-                    uint16_t* scratch_words /* >= O_BLOCK_WORDS */) {
+                    uint16_t* scratch_words /* >= 2 * O_BLOCK_WORDS: decoded words, then raw low bits */) {
+  uint16_t* raw_low = scratch_words + O_BLOCK_WORDS;
   const uint32_t n = b->nbytes;
   if (b->kind == O_RAW) {
     if (b->clen < n) return O_ERR_BOUNDS;
@@ -167,9 +177,25 @@ int wso_apply_block(const o_block* b, const uint8_t* payload, const uint32_t* ta
   else
     return O_ERR_KIND;
   const int xor_apply = b->kind == O_ANS_XOR || b->kind == O_DICT_XOR;
+  const int dict = b->kind == O_DICT_XOR || b->kind == O_DICT_U16;
   const uint32_t W = n / 2;
-  if ((b->kind == O_DICT_XOR || b->kind == O_DICT_U16) && (b->flags & 2u)) {
-    const uint32_t side = (2u * b->nwords + 15u) & ~15u;
+  uint32_t side = (2u * b->nwords + 15u) & ~15u;
+  const uint32_t split_code = (b->flags >> 2) & 3u;
+  if (split_code && !dict) return err | O_ERR_KIND;
+  if (split_code) {
+    const uint32_t k = split_code == 3u ? 4u : split_code, per = 4u / k;
+    const uint32_t groups = (W + 255u) / 256u;
+    const uint64_t raw_bytes = 128ull * ((groups + per - 1u) / per);
+    if ((uint64_t)side + raw_bytes > b->clen) return err | O_ERR_LENGTH;
+    for (uint32_t i = 0; i < W; ++i) {
+      const uint32_t g = i / 256u, l = (i % 256u) / 8u, j = i % 8u;
+      const uint32_t rw = rd32(payload + side + 4u * ((g / per) * 32u + l));
+      const uint32_t bit = ((j & 1u) ? 16u : 0u) + (g % per) * 4u * k + (j / 2u) * k;
+      raw_low[i] = (uint16_t)((rw >> bit) & ((1u << k) - 1u));
+    }
+    side += (uint32_t)raw_bytes;
+  }
+  if (dict && (b->flags & 2u)) {
     if ((uint64_t)side + 64 > b->clen) return err | O_ERR_LENGTH;
     uint32_t at = side + 64;
     for (uint32_t l = 0; l < 32; ++l) {
@@ -185,6 +211,8 @@ int wso_apply_block(const o_block* b, const uint8_t* payload, const uint32_t* ta
       }
     }
   }
+  if (split_code)
+    for (uint32_t i = 0; i < W; ++i) scratch_words[i] |= raw_low[i];
   for (uint32_t i = 0; i < W; ++i) {
     uint16_t old = rd16(dst + 2 * i), nw;
     if (xor_apply) {
@@ -250,7 +278,7 @@ typedef struct {
 
 static void* o_worker(void* arg) {
   o_job* j = (o_job*)arg;
-  static __thread uint16_t words[O_BLOCK_WORDS];
+  static __thread uint16_t words[2 * O_BLOCK_WORDS];
   for (uint64_t t = (uint64_t)j->tid; t < j->ntiles; t += (uint64_t)j->nthreads) {
     const o_tile* tile = &j->tiles[t];
     const uint32_t* table = tile->table == 0xFFFFFFFFu ? 0 : j->tables + 512ull * tile->table;

@@ -168,7 +168,9 @@ def _fuzz_strategies() -> dict:
         transform=st.sampled_from(["xor", "u16"]),
         odd=st.booleans(),
         policy=st.sampled_from(["auto", "xor", "u16"]),
-        coding=st.sampled_from([(-1, -1), (6, 0), (100, -1), (100, 1)]),  # (dict_slack_pct, escapes)
+        # (dict_slack_pct, escapes, split)
+        coding=st.sampled_from([(-1, -1, -1), (6, 0, 0), (100, -1, -1), (100, 1, -1), (100, -1, 1), (100, 0, 2),
+                                (100, 1, 4)]),
         seed=st.integers(0, 2**31 - 1),
     )
 
@@ -177,8 +179,8 @@ def _fuzz_strategies() -> dict:
 FUZZ = _fuzz_strategies()
 
 
-def host_plan(a: dict[str, torch.Tensor], b: dict[str, torch.Tensor], policy: str, threads: int = 4, dict_slack_pct: int = 6,
-              escapes: int = 0):
+def host_plan(a: dict[str, torch.Tensor], b: dict[str, torch.Tensor], policy: str, dict_slack_pct: int = 6,
+              escapes: int = 0, split: int = 0, threads: int = 4):
     """Build a plan on host targets (no GPU); b's tensors are the destinations."""
     lib = _lib.load()
     descs = (_lib.TensorDesc * len(a))()
@@ -189,7 +191,7 @@ def host_plan(a: dict[str, torch.Tensor], b: dict[str, torch.Tensor], policy: st
         )
     opts = _lib.BuildOptions(policy=_lib.POLICIES[policy], threads=threads, target_on_device=0, device=0,
                              batch_bytes=0, staging_slots=0, pin_arena=0, dict_slack_pct=dict_slack_pct,
-                             escapes=escapes)
+                             escapes=escapes, split=split)
     plan = ctypes.c_void_p()
     _lib.check(lib.ws_plan_build(descs, len(a), ctypes.byref(opts), None, ctypes.byref(plan)))
     return plan
@@ -211,6 +213,26 @@ def plan_arrays(plan) -> tuple[np.ndarray, np.ndarray, np.ndarray, np.ndarray, _
     tables = arr(view.tables, 4 * 512 * view.ntables, np.uint32)
     arena = arr(view.arena, view.arena_bytes, np.uint8)
     return blocks, tiles, tables, arena, stats
+
+
+def split_bits(flags: int) -> int:
+    """Raw low bits per word of a split-word block (flags bits 2-3: 0, 1, 2, 4)."""
+    return (0, 1, 2, 4)[(int(flags) >> 2) & 3]
+
+
+def split_raw_bytes(words: int, k: int) -> int:
+    """Bytes of a split-word block's raw section: one uint32 per lane per 4 / k groups."""
+    if not k:
+        return 0
+    groups = (words + 255) // 256
+    per = 4 // k
+    return 128 * ((groups + per - 1) // per)
+
+
+def escape_list_offset(blk) -> int:
+    """Arena offset of a dictionary block's escape list (after the stream and any raw section)."""
+    return (int(blk["src"]) + ((2 * int(blk["nwords"]) + 15) & ~15)
+            + split_raw_bytes(int(blk["nbytes"]) // 2, split_bits(blk["flags"])))
 
 
 def as_bytes(t: torch.Tensor) -> np.ndarray:

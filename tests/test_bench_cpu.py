@@ -40,7 +40,7 @@ def test_both_arms_name_the_workload_with_the_same_config() -> None:
     spec, desc = bench.workload_spec(args, 2, 0)
     cfg = bench.workload_config(args, desc, spec.nbytes)
     assert cfg == bench.workload_config(args, desc, spec.nbytes)
-    assert set(cfg) == {"workload", "policy", "scale", "escapes", "l2"}
+    assert set(cfg) == {"workload", "policy", "scale", "escapes", "split", "l2"}
     assert "tp=2" in cfg["workload"] and spec.tp == 2
 
 
@@ -65,7 +65,7 @@ def test_reference_arm_runs_on_host_cores_without_product_code() -> None:
     line = json.loads(lines[0])
     assert line["impl"] == "reference" and line["value"] > 0 and line["e2e"]["h2d_bytes_per_step"] == 0
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
-    assert set(line["config"]) == {"workload", "policy", "scale", "escapes", "l2"}
+    assert set(line["config"]) == {"workload", "policy", "scale", "escapes", "split", "l2"}
     assert "NO_PRODUCT_LIBRARY" in out.stdout
 
 

@@ -17,7 +17,8 @@ import torch
 
 from oracle import semantics as sem
 from oracle import stream as ostream
-from tests.helpers import adversarial_pair, as_bytes, bf16_pair, edge_pair, host_plan, plan_arrays
+from tests.helpers import (adversarial_pair, as_bytes, bf16_pair, edge_pair, escape_list_offset, host_plan,
+                           plan_arrays, split_bits, split_raw_bytes)
 from warpshift_b200 import _lib
 
 KIND_RAW, KIND_XOR, KIND_U16, KIND_DICT_XOR, KIND_DICT_U16 = 0, 1, 2, 3, 4
@@ -27,9 +28,12 @@ def clone(d):
     return {k: v.clone() for k, v in d.items()}
 
 
-# (dict_slack_pct, escapes): byte planes only, the default choice, a dictionary
-# wherever possible, and dictionaries with escape lists wherever eligible.
-CODINGS = {"planes": (-1, -1), "default": (6, 0), "dictionary": (100, -1), "escapes": (100, 1)}
+# (dict_slack_pct, escapes, split): byte planes only, the default choice, a
+# dictionary wherever possible, dictionaries with escape lists wherever
+# eligible, and split-word dictionaries of k = 1, 2, 4 raw bits wherever
+# eligible (k = 4 with escapes).
+CODINGS = {"planes": (-1, -1, -1), "default": (6, 0, 0), "dictionary": (100, -1, -1), "escapes": (100, 1, -1),
+           "split1": (100, -1, 1), "split2": (100, 0, 2), "split4": (100, 1, 4)}
 
 
 @pytest.mark.parametrize("coding", list(CODINGS))
@@ -37,7 +41,7 @@ CODINGS = {"planes": (-1, -1), "default": (6, 0), "dictionary": (100, -1), "esca
 def test_host_plan_round_trips_through_the_oracle_decoder(policy: str, coding: str) -> None:
     a, b = edge_pair(seed=7)
     work = clone(b)
-    plan = host_plan(a, work, policy, dict_slack_pct=CODINGS[coding][0], escapes=CODINGS[coding][1])
+    plan = host_plan(a, work, policy, *CODINGS[coding])
     try:
         blocks, tiles, tables, arena, stats = plan_arrays(plan)
         assert stats.runtime_bytes == sum(t.numel() * t.element_size() for t in b.values())
@@ -71,7 +75,7 @@ def blocks_by_tensor(blocks, work) -> dict[str, list]:
 def test_boundary_residuals_round_trip_through_the_oracle_decoder(adversarial, policy: str, coding: str) -> None:
     a, b = adversarial
     work = clone(b)
-    plan = host_plan(a, work, policy, dict_slack_pct=CODINGS[coding][0], escapes=CODINGS[coding][1])
+    plan = host_plan(a, work, policy, *CODINGS[coding])
     try:
         blocks, tiles, tables, arena, stats = plan_arrays(plan)
         for reverse, teacher in ((True, a), (False, b), (True, a)):
@@ -90,7 +94,7 @@ def test_dictionary_and_escape_limits_are_exact(adversarial, policy: str, suffix
     escapes, and a block that needs more is carried raw."""
     a, b = adversarial
     work = clone(b)
-    plan = host_plan(a, work, policy, dict_slack_pct=100, escapes=1)
+    plan = host_plan(a, work, policy, dict_slack_pct=100, escapes=1, split=-1)
     try:
         blocks, tiles, tables, arena, stats = plan_arrays(plan)
         by = blocks_by_tensor(blocks, work)
@@ -99,7 +103,7 @@ def test_dictionary_and_escape_limits_are_exact(adversarial, policy: str, suffix
         assert dict_kind not in kinds[f"distinct_256_{suffix}"]
         first, second = by[f"lane5_escapes_64_{suffix}"]
         assert first["kind"] == dict_kind and first["flags"] & 2
-        side = int(first["src"]) + ((2 * int(first["nwords"]) + 15) & ~15)
+        side = escape_list_offset(first)
         counts = arena[side : side + 64].view(np.uint16)
         assert counts[5] == 64 and counts.sum() == 64
         first, second = by[f"lane5_escapes_126_{suffix}"]
@@ -156,7 +160,7 @@ def test_mode_rule_follows_the_reference() -> None:
 def test_coded_words_are_the_reference_residual(policy: str, coding: str) -> None:
     a_t, b_t = bf16_pair(3 * 32768 + 1000, 0.01, 9)
     a, b = {"w": a_t}, {"w": b_t.clone()}
-    plan = host_plan(a, b, policy, dict_slack_pct=CODINGS[coding][0], escapes=CODINGS[coding][1])
+    plan = host_plan(a, b, policy, *CODINGS[coding])
     try:
         blocks, tiles, tables, arena, stats = plan_arrays(plan)
         base, target = as_bytes(a_t), as_bytes(b_t)
@@ -208,7 +212,7 @@ def test_escape_lists_shrink_the_stream_and_malformed_lists_are_reported() -> No
     sizes = {}
     for esc in (-1, 0):
         work = {"w": b_t.clone()}
-        plan = host_plan({"w": a_t}, work, "xor", escapes=esc)
+        plan = host_plan({"w": a_t}, work, "xor", escapes=esc, split=-1)
         try:
             blocks, tiles, tables, arena, stats = plan_arrays(plan)
             sizes[esc] = int(stats.arena_bytes)
@@ -217,7 +221,7 @@ def test_escape_lists_shrink_the_stream_and_malformed_lists_are_reported() -> No
             np.testing.assert_array_equal(as_bytes(work["w"]), as_bytes(a_t))
             if esc == 0:
                 blk = escape_block(blocks)
-                side = int(blk["src"]) + ((2 * int(blk["nwords"]) + 15) & ~15)
+                side = escape_list_offset(blk)
                 counts = arena[side: side + 64].view(np.uint16)
                 lane = next(l for l in range(31) if counts[l + 1] > 0)
                 counts[lane] += 1  # lane now reads the next lane's first entry
@@ -296,4 +300,89 @@ def test_dictionary_needs_few_distinct_words_and_planes_cover_the_rest() -> None
             assert kinds == {KIND_DICT_XOR}
         else:
             assert KIND_DICT_XOR not in kinds
+        _lib.load().ws_plan_destroy(plan)
+
+
+def test_split_words_shrink_the_stream_where_low_bits_are_noise() -> None:
+    """Split-word dictionaries (the low k bits of each word stored raw, the rest
+    coded) are chosen when estimated smaller: XOR s = 0.01 codes with k = 1,
+    XOR s = 0.1 moves from byte planes to a k = 4 dictionary, U16 s = 0.1 takes
+    k = 4; every plan decodes exactly through the oracle."""
+    cases = [("xor", 0.01, 1, 0.99), ("xor", 0.1, 4, 0.90), ("u16", 0.1, 4, 0.985)]
+    for policy, scale, k, bound in cases:
+        a_t, b_t = bf16_pair(1 << 20, scale, 21)
+        sizes = {}
+        for split in (-1, 0):
+            work = {"w": b_t.clone()}
+            plan = host_plan({"w": a_t}, work, policy, split=split)
+            try:
+                blocks, tiles, tables, arena, stats = plan_arrays(plan)
+                sizes[split] = int(stats.arena_bytes)
+                coded = blocks[blocks["kind"] != KIND_RAW]
+                assert {split_bits(f) for f in coded["flags"]} == ({0} if split < 0 else {k}), (policy, scale)
+                if split == 0:
+                    assert set(coded["kind"]) <= {KIND_DICT_XOR, KIND_DICT_U16}
+                err, ck = ostream.apply_plan(blocks, tiles, tables, arena, 0, True, 2)
+                assert err == 0 and ck == stats.expected_checksum[1]
+                np.testing.assert_array_equal(as_bytes(work["w"]), as_bytes(a_t))
+            finally:
+                _lib.load().ws_plan_destroy(plan)
+        assert sizes[0] < sizes[-1] * bound, (policy, scale, sizes)
+
+
+def residual_words(a_t: torch.Tensor, b_t: torch.Tensor, policy: str) -> np.ndarray:
+    a = a_t.view(torch.int16).numpy().view(np.uint16).astype(np.int64)
+    b = b_t.view(torch.int16).numpy().view(np.uint16).astype(np.int64)
+    if policy == "xor":
+        return (a ^ b).astype(np.uint16)
+    d = ((b - a + 32768) & 0xFFFF) - 32768  # delta.py:26-34, then the coded rotation
+    z = ((d << 1) ^ (d >> 15)) & 0xFFFF
+    return (((z >> 1) | ((z & 1) << 15)) & 0xFFFF).astype(np.uint16)
+
+
+@pytest.mark.parametrize("k", [1, 2, 4])
+@pytest.mark.parametrize("policy", ["xor", "u16"])
+def test_split_raw_section_holds_each_words_low_bits(policy: str, k: int) -> None:
+    """The raw section of every split block, read back by the layout's own rule
+    (raw word (g / G) * 32 + lane, G = 4 / k, bit (g % G) * 4k + (j odd) * 16 +
+    (j / 2) * k), equals the low k bits of the reference residual words; a
+    flipped raw bit changes exactly that word of the applied result."""
+    a_t, b_t = bf16_pair(70001, 0.01, 22)  # a partial last group and block
+    work = {"w": b_t.clone()}
+    plan = host_plan({"w": a_t}, work, policy, dict_slack_pct=100, split=k)
+    try:
+        blocks, tiles, tables, arena, stats = plan_arrays(plan)
+        r = residual_words(a_t, b_t, policy)
+        per, mask = 4 // k, (1 << k) - 1
+        checked = 0
+        for blk in blocks:
+            if blk["kind"] == KIND_RAW:
+                continue
+            assert split_bits(blk["flags"]) == k
+            W = int(blk["nbytes"]) // 2
+            first = (int(blk["dst"]) - work["w"].data_ptr()) // 2  # host targets: dst is a host address
+            off = int(blk["src"]) + ((2 * int(blk["nwords"]) + 15) & ~15)
+            raw = arena[off: off + split_raw_bytes(W, k)].view(np.uint32)
+            w = np.arange(W)
+            g, lane, j = w // 256, (w % 256) // 8, w % 8
+            bit = (j & 1) * 16 + (g % per) * 4 * k + (j // 2) * k
+            got = (raw[(g // per) * 32 + lane] >> bit.astype(np.uint32)) & mask
+            np.testing.assert_array_equal(got, r[first: first + W] & mask)
+            checked += 1
+        assert checked >= 1
+        blk = next(bk for bk in blocks if bk["kind"] != KIND_RAW)
+        off = int(blk["src"]) + ((2 * int(blk["nwords"]) + 15) & ~15)
+        word = 256 * 3 + 8 * 7 + 5  # group 3, lane 7, lane word 5 (odd: high half)
+        g, lane, j = 3, 7, 5
+        bit = 16 + (g % per) * 4 * k + (j // 2) * k
+        raw = arena[off: off + split_raw_bytes(int(blk["nbytes"]) // 2, k)].view(np.uint32)
+        raw[(g // per) * 32 + lane] ^= np.uint32(1 << bit)
+        err, ck = ostream.apply_plan(blocks, tiles, tables, arena, 0, True, 2)
+        assert err == 0 and ck != stats.expected_checksum[1]
+        first = (int(blk["dst"]) - work["w"].data_ptr()) // 2
+        got = work["w"].view(torch.int16).numpy().view(np.uint16)
+        want = a_t.view(torch.int16).numpy().view(np.uint16)
+        bad = np.nonzero(got != want)[0]
+        assert list(bad) == [first + word]
+    finally:
         _lib.load().ws_plan_destroy(plan)

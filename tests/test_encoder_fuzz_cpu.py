@@ -22,7 +22,7 @@ from warpshift_b200 import _lib
 def test_random_residuals_round_trip_through_the_oracle_decoder(size_class, kind, param, transform, odd, policy, coding, seed):
     a, b = random_pair(size_class, kind, param, transform, odd, seed)
     work = {k: v.clone() for k, v in b.items()}
-    plan = host_plan(a, work, policy, dict_slack_pct=coding[0], escapes=coding[1])
+    plan = host_plan(a, work, policy, *coding)
     try:
         blocks, tiles, tables, arena, stats = plan_arrays(plan)
         for reverse, teacher in ((True, a), (False, b)):

@@ -21,7 +21,7 @@ pytestmark = pytest.mark.gpu
 
 
 def build(a, b_dev, policy, slack, on_device, encode_batch_bytes=0, pin_arena=0, batch_bytes=0, escapes=0,
-          host_fallback=0):
+          host_fallback=0, split=0):
     lib = _lib.load()
     descs = (_lib.TensorDesc * len(a))()
     for i, name in enumerate(b_dev):
@@ -31,7 +31,7 @@ def build(a, b_dev, policy, slack, on_device, encode_batch_bytes=0, pin_arena=0,
     opts = _lib.BuildOptions(policy=_lib.POLICIES[policy], threads=4, target_on_device=1, device=0,
                              batch_bytes=batch_bytes, staging_slots=0, pin_arena=pin_arena, dict_slack_pct=slack,
                              encode_on_device=int(on_device), encode_batch_bytes=encode_batch_bytes,
-                             escapes=escapes, host_fallback=host_fallback)
+                             escapes=escapes, host_fallback=host_fallback, split=split)
     plan = ctypes.c_void_p()
     stream = torch.cuda.current_stream().cuda_stream
     _lib.check(lib.ws_plan_build(descs, len(a), ctypes.byref(opts), stream, ctypes.byref(plan)))
@@ -51,14 +51,19 @@ def assert_same_plan(p_gpu, p_host) -> None:
     np.testing.assert_array_equal(ag, ah)
 
 
-@pytest.mark.parametrize("slack, escapes", [(-1, -1), (6, 0), (100, -1), (100, 1)])
+# (dict_slack_pct, escapes, split): planes only, the defaults, plain and escaped
+# dictionaries, and split-word dictionaries of k = 1, 2, 4 raw bits.
+CODINGS = [(-1, -1, -1), (6, 0, 0), (100, -1, -1), (100, 1, -1), (100, -1, 1), (100, 0, 2), (100, 1, 4)]
+
+
+@pytest.mark.parametrize("slack, escapes, split", CODINGS)
 @pytest.mark.parametrize("policy", ["auto", "xor", "u16"])
-def test_gpu_encoder_matches_host_encoder(cuda_device, policy: str, slack: int, escapes: int) -> None:
+def test_gpu_encoder_matches_host_encoder(cuda_device, policy: str, slack: int, escapes: int, split: int) -> None:
     a, b = edge_pair(seed=13)
     b_dev = {k: v.to(cuda_device) for k, v in b.items()}
     lib = _lib.load()
-    p_gpu = build(a, b_dev, policy, slack, True, escapes=escapes)
-    p_host = build(a, b_dev, policy, slack, False, escapes=escapes)
+    p_gpu = build(a, b_dev, policy, slack, True, escapes=escapes, split=split)
+    p_host = build(a, b_dev, policy, slack, False, escapes=escapes, split=split)
     try:
         assert_same_plan(p_gpu, p_host)
     finally:
@@ -71,17 +76,17 @@ def adversarial():
     return adversarial_pair(seed=5)
 
 
-@pytest.mark.parametrize("slack, escapes", [(-1, -1), (6, 0), (100, 1)])
+@pytest.mark.parametrize("slack, escapes, split", [(-1, -1, -1), (6, 0, 0), (100, 1, -1), (100, 1, 1), (100, 0, 4)])
 @pytest.mark.parametrize("policy", ["auto", "xor", "u16"])
 def test_gpu_encoder_matches_host_encoder_on_coding_limits(cuda_device, adversarial, policy: str, slack: int,
-                                                          escapes: int) -> None:
+                                                          escapes: int, split: int) -> None:
     """255/256 distinct words (the device word table's limit), a lane's escape
     list at 64 entries and past it, extreme skew, an exact 16 MiB packet."""
     a, b = adversarial
     b_dev = {k: v.to(cuda_device) for k, v in b.items()}
     lib = _lib.load()
-    p_gpu = build(a, b_dev, policy, slack, True, escapes=escapes)
-    p_host = build(a, b_dev, policy, slack, False, escapes=escapes)
+    p_gpu = build(a, b_dev, policy, slack, True, escapes=escapes, split=split)
+    p_host = build(a, b_dev, policy, slack, False, escapes=escapes, split=split)
     try:
         assert_same_plan(p_gpu, p_host)
     finally:
@@ -190,6 +195,38 @@ def test_gpu_encoder_under_memory_pressure(cuda_device, leave_mb: int, encoder: 
         _lib.check(lib.ws_plan_get_stats(p_gpu, ctypes.byref(stats)))
         assert _lib.ENCODERS[stats.encoder] == encoder
         assert_same_plan(p_gpu, p_host)
+    finally:
+        lib.ws_plan_destroy(p_gpu)
+        lib.ws_plan_destroy(p_host)
+
+
+@pytest.mark.parametrize("policy, scale, ks", [("xor", 0.01, {1}), ("xor", 0.1, {4}), ("u16", 0.1, {2, 4})])
+def test_split_words_on_teacher_like_residuals(cuda_device, policy: str, scale: float, ks: set) -> None:
+    """The default coding of relative-noise BF16 pairs splits words (k = 1 at
+    XOR s = 0.01, k = 4 at XOR s = 0.1; U16 s = 0.1 estimates k = 2 and k = 4
+    within 0.1 % of each other): both encoders give the same plan, and the
+    kernel switches B -> A -> B exactly."""
+    from tests.helpers import split_bits
+
+    x, y = bf16_pair((24 << 20) // 2 + 4097, scale, 41)  # two packets, partial last block and group
+    b_dev = {"w": y.to(cuda_device)}
+    lib = _lib.load()
+    p_gpu = build({"w": x}, b_dev, policy, 6, True, pin_arena=1)
+    p_host = build({"w": x}, b_dev, policy, 6, False)
+    try:
+        assert_same_plan(p_gpu, p_host)
+        blocks = plan_arrays(p_gpu)[0]
+        coded = blocks[blocks["kind"] != 0]
+        assert {split_bits(f) for f in coded["flags"]} <= ks
+        stream = torch.cuda.current_stream().cuda_stream
+        _lib.check(lib.ws_plan_upload(p_gpu, stream))
+        res = _lib.ApplyResult()
+        _lib.check(lib.ws_apply(p_gpu, 1, stream, None, ctypes.byref(res)))  # B -> A
+        assert res.checksum == res.expected and res.device_errors == 0
+        assert torch.equal(b_dev["w"].cpu().view(torch.int16), x.view(torch.int16))
+        _lib.check(lib.ws_apply(p_gpu, 0, stream, None, ctypes.byref(res)))  # A -> B
+        assert res.checksum == res.expected
+        assert torch.equal(b_dev["w"].cpu().view(torch.int16), y.view(torch.int16))
     finally:
         lib.ws_plan_destroy(p_gpu)
         lib.ws_plan_destroy(p_host)

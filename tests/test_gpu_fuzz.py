@@ -24,7 +24,7 @@ def test_random_residuals_round_trip_on_the_gpu(cuda_device, size_class, kind, p
                                                 seed):
     a, b = random_pair(size_class, kind, param, transform, odd, seed)
     gpu = {k: v.to(cuda_device) for k, v in b.items()}
-    delta = DeltaWeights(a, gpu, policy=policy, dict_slack_pct=coding[0], escapes=coding[1])
+    delta = DeltaWeights(a, gpu, policy=policy, dict_slack_pct=coding[0], escapes=coding[1], split=coding[2])
     try:
         for reverse, expected in ((True, a), (False, b)):
             delta.apply(reverse=reverse)

@@ -229,7 +229,7 @@ def test_malformed_escape_list_is_reported(cuda_device) -> None:
     import ctypes
 
     from oracle import stream as ostream
-    from tests.helpers import bf16_pair
+    from tests.helpers import bf16_pair, escape_list_offset
 
     x, y = bf16_pair(1 << 20, 0.01, 12)
     gpu = {"w": y.to(cuda_device)}
@@ -238,7 +238,7 @@ def test_malformed_escape_list_is_reported(cuda_device) -> None:
     blocks = np.ctypeslib.as_array((ctypes.c_uint8 * (32 * view.nblocks)).from_address(view.blocks)).view(ostream.BLOCK_DTYPE)
     arena = np.ctypeslib.as_array((ctypes.c_uint8 * view.arena_bytes).from_address(view.arena))
     blk = next(bk for bk in blocks if bk["flags"] & 2)
-    side = int(blk["src"]) + ((2 * int(blk["nwords"]) + 15) & ~15)
+    side = escape_list_offset(blk)
     counts = arena[side: side + 64].view(np.uint16)
     lane = next(l for l in range(31) if counts[l + 1] > 0)
     counts[lane] += 1  # lane now reads the next lane's first entry

@@ -38,6 +38,7 @@ class BuildOptions(ctypes.Structure):
         ("encode_batch_bytes", u64),
         ("escapes", i32),
         ("host_fallback", i32),
+        ("split", i32),
     ]
 
 

@@ -393,9 +393,11 @@ struct EscapeCursor {
   bool bad = false;
 
   // Reads the lane counts (global, so the latency overlaps the first ring copy)
-  // and the lane's first entry. A list that does not fit the payload is bad.
-  __device__ __forceinline__ void open(const ws_block_desc& bd, const uint8_t* __restrict__ src, uint32_t lane) {
-    const uint32_t side = (2u * bd.nwords + 15u) & ~15u;
+  // and the lane's first entry; the list starts `raw_bytes` (a split-word
+  // block's raw section) after the stream. A list that does not fit the payload is bad.
+  __device__ __forceinline__ void open(const ws_block_desc& bd, const uint8_t* __restrict__ src, uint32_t lane,
+                                       uint32_t raw_bytes) {
+    const uint32_t side = ((2u * bd.nwords + 15u) & ~15u) + raw_bytes;
     bad = side + WS_ESCAPE_HEADER_BYTES > bd.clen;
     uint32_t mine = 0, incl = 0;
     if (!bad) mine = reinterpret_cast<const uint16_t*>(src + side)[lane];
@@ -439,9 +441,33 @@ struct EscapeCursor {
   }
 };
 
-template <bool U16, bool REVERSE, bool DICT, bool FIXED_BASE>
+// Split-word blocks (SPLIT, dictionary kinds only): the low k bits of each
+// word come from the raw section after the stream (WS_FLAG_SPLIT_MASK layout in
+// ws_format.h), read with plain cached loads: one uint32 per lane covers 4 / k
+// groups, and one shift and mask per word pair put its bits in place.
+struct SplitRaw {
+  uint32_t off = 0;  // byte offset of the lane's first raw word in the payload
+  uint32_t k = 0;    // raw bits per word
+
+  // The raw word holding group g's bits and the bit offset of group g in it.
+  __device__ __forceinline__ uint32_t load(const uint8_t* __restrict__ src, uint32_t g) const {
+    return __ldg(reinterpret_cast<const uint32_t*>(src + off) + ((g * k) >> 2) * WS_LANES);
+  }
+  __device__ __forceinline__ uint32_t offset(uint32_t g) const { return ((g * k) & 3u) << 2; }
+  __device__ __forceinline__ void merge(uint32_t rw, uint32_t o, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) const {
+    const uint32_t mask2 = (0x00010001u << k) - 0x00010001u;  // k low bits of both 16-bit halves
+    r0 |= (rw >> o) & mask2;
+    r1 |= (rw >> (o + k)) & mask2;
+    r2 |= (rw >> (o + 2u * k)) & mask2;
+    r3 |= (rw >> (o + 3u * k)) & mask2;
+  }
+};
+
+template <bool U16, bool REVERSE, bool DICT, bool FIXED_BASE, bool SPLIT = false>
 __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t* __restrict__ src, uint32_t tbase,
                           uint8_t* ring, uint32_t bar_base, uint32_t lane, ws_device_result* res) {
+  static_assert(DICT || !SPLIT, "only word-dictionary blocks split words");
   uint8_t* dst = reinterpret_cast<uint8_t*>(bd.dst);
   const uint32_t n = bd.nbytes;
   const uint32_t W = n / 2;
@@ -449,8 +475,23 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
   const uint32_t dec_groups = (W + WS_GROUP_WORDS - 1) / WS_GROUP_WORDS;
   const uint32_t groups = (n + WS_GROUP_BYTES - 1) / WS_GROUP_BYTES;
   const bool aligned = (bd.dst & 15u) == 0;
-  // Only the stream goes through the ring; an escape list is read from global memory.
-  const uint32_t staged = (DICT && (bd.flags & WS_FLAG_ESCAPES)) ? min(bd.clen, (2u * bd.nwords + 15u) & ~15u) : bd.clen;
+  const uint32_t stream_bytes = (2u * bd.nwords + 15u) & ~15u;
+  SplitRaw split;
+  uint32_t raw_bytes = 0;
+  if (SPLIT) {
+    split.k = ws_split_bits(bd.flags);
+    raw_bytes = ws_split_raw_bytes(W, split.k);
+    // The raw section must lie inside the payload; nothing is read or written otherwise.
+    if ((uint64_t)stream_bytes + raw_bytes > bd.clen) {
+      if (lane == 0) report(res, WS_DEVERR_LENGTH, block);
+      return;
+    }
+    split.off = stream_bytes + 4u * lane;
+  }
+  // Only the stream goes through the ring; a raw section and an escape list are
+  // read from global memory.
+  const uint32_t staged =
+      (DICT && (bd.flags & (WS_FLAG_ESCAPES | WS_FLAG_SPLIT_MASK))) ? min(bd.clen, stream_bytes) : bd.clen;
   const uint32_t total_halves = (staged + WS_RING_HALF_BYTES - 1) / WS_RING_HALF_BYTES;
   const uint32_t ring_s = smem_addr(ring);
   const uint32_t ltm = lanemask_lt();
@@ -476,7 +517,7 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
   issue(0);
   issue(1);
   EscapeCursor esc;
-  if (DICT && (bd.flags & WS_FLAG_ESCAPES)) esc.open(bd, src, lane);
+  if (DICT && (bd.flags & WS_FLAG_ESCAPES)) esc.open(bd, src, lane, raw_bytes);
   uint32_t ready = 0;
   bool ok = true;
   if (total_halves > 0) {
@@ -520,7 +561,9 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
   };
   // The lane's word pairs r0..r3 of group `grp` applied to the destination
   // vector `old` (escaped words patched in first) and written back.
-  auto finish = [&](uint4* q, uint4 old, uint32_t grp, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+  auto finish = [&](uint4* q, uint4 old, uint32_t grp, uint32_t rw, uint32_t r0, uint32_t r1, uint32_t r2,
+                    uint32_t r3) {
+    if (SPLIT) split.merge(rw, split.offset(grp), r0, r1, r2, r3);
     if (DICT && esc.w < (grp + 1) * WS_GROUP_WORDS) esc.patch(grp, lane, r0, r1, r2, r3);
     uint4 v;
     if (U16) {
@@ -552,6 +595,7 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
       if (pos >= next_event && !at_event()) break;
       const uint4 old0 = ldg128_early(p);
       const uint4 old1 = ldg128_early(p + WS_GROUP_BYTES / 16);
+      const uint32_t rw0 = SPLIT ? split.load(src, g) : 0u, rw1 = SPLIT ? split.load(src, g + 1) : 0u;
       if (lane == 0 && g + 2 + kPrefetchGroups + 2 <= fast_groups)
         prefetch_l2(dst + (g + 2 + kPrefetchGroups) * WS_GROUP_BYTES, 2 * WS_GROUP_BYTES);
       uint32_t rp = ring_s + (pos & (kRingHalfwords - 1)) * 2u;
@@ -559,10 +603,10 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
       uint32_t r0, r1, r2, r3;
       check_dict<FIXED_BASE>(xa, xb, rp, tbase, lba, ltm, r0, r1);
       check_dict<FIXED_BASE>(xa, xb, rp, tbase, lba, ltm, r2, r3);
-      finish(p, old0, g, r0, r1, r2, r3);
+      finish(p, old0, g, rw0, r0, r1, r2, r3);
       check_dict<FIXED_BASE>(xa, xb, rp, tbase, lba, ltm, r0, r1);
       check_dict<FIXED_BASE>(xa, xb, rp, tbase, lba, ltm, r2, r3);
-      finish(p + WS_GROUP_BYTES / 16, old1, g + 1, r0, r1, r2, r3);
+      finish(p + WS_GROUP_BYTES / 16, old1, g + 1, rw1, r0, r1, r2, r3);
       pos += (rp - rp0) >> 1;
     }
   }
@@ -573,6 +617,7 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
   for (; ok && g < fast_groups; ++g, p += WS_GROUP_BYTES / 16) {
     if (pos >= next_event && !at_event()) break;
     const uint4 old = DICT ? ldg128_early(p) : *p;
+    const uint32_t rw = SPLIT ? split.load(src, g) : 0u;
     uint32_t rp = ring_s + (pos & (kRingHalfwords - 1)) * 2u;
     const uint32_t rp0 = rp;
     uint32_t r0, r1, r2, r3;
@@ -586,7 +631,7 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
       r3 = check_fast<FIXED_BASE>(xa, xb, rp, tbase, lba, lbb, ltm);
     }
     pos += (rp - rp0) >> 1;
-    finish(p, old, g, r0, r1, r2, r3);
+    finish(p, old, g, rw, r0, r1, r2, r3);
   }
 
   // Generic path: the partial last group, the uncoded odd tail byte, and
@@ -625,6 +670,7 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
       }
     }
     uint32_t out[4] = {0, 0, 0, 0};
+    if (SPLIT && g < dec_groups) split.merge(split.load(src, g), split.offset(g), r[0], r[1], r[2], r[3]);
     if (DICT && g < dec_groups) esc.patch(g, lane, r[0], r[1], r[2], r[3]);
     apply_chunk_bytes<U16, REVERSE>(dst + off, off, n, r, coded_bytes, bd.tail, out);
     ck.add(out[0], out[1], out[2], out[3]);
@@ -667,16 +713,26 @@ __device__ __forceinline__ void run_block(const ws_block_desc& bd, uint32_t bloc
       raw_block(bd, block, src, lane, res);
       break;
     case WS_KIND_ANS_XOR:
-      ans_block<false, REVERSE, false, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
-      break;
     case WS_KIND_ANS_U16:
-      ans_block<true, REVERSE, false, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
+      if (bd.flags & WS_FLAG_SPLIT_MASK) {  // byte planes never split words
+        if (lane == 0) report(res, WS_DEVERR_KIND, block);
+      } else if (bd.kind == WS_KIND_ANS_XOR) {
+        ans_block<false, REVERSE, false, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
+      } else {
+        ans_block<true, REVERSE, false, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
+      }
       break;
     case WS_KIND_DICT_XOR:
-      ans_block<false, REVERSE, true, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
+      if (bd.flags & WS_FLAG_SPLIT_MASK)
+        ans_block<false, REVERSE, true, FIXED_BASE, true>(bd, block, src, tbase, ring, bar_base, lane, res);
+      else
+        ans_block<false, REVERSE, true, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
       break;
     case WS_KIND_DICT_U16:
-      ans_block<true, REVERSE, true, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
+      if (bd.flags & WS_FLAG_SPLIT_MASK)
+        ans_block<true, REVERSE, true, FIXED_BASE, true>(bd, block, src, tbase, ring, bar_base, lane, res);
+      else
+        ans_block<true, REVERSE, true, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
       break;
     default:
       if (lane == 0) report(res, WS_DEVERR_KIND, block);
@@ -859,14 +915,24 @@ std::mutex g_noalloc_mutex;
 ws_device_result* g_noalloc_ptr[kMaxDevices] = {};
 
 // Device address of g_noalloc_scratch on `device` (which must be current).
-// Host code cannot use the symbol itself: it names a host-side shadow.
+// Host code cannot use the symbol itself: it names a host-side shadow. The
+// first call on a device also loads every kernel a later call launches (both
+// directions and the reduction) and sets their shared-memory limit: with lazy
+// module loading a kernel is otherwise loaded, and memory for it allocated, at
+// its first launch, which may be a later call.
 int noalloc_scratch(int device, ws_device_result** out) {
   std::lock_guard<std::mutex> lk(g_noalloc_mutex);
   if (!g_noalloc_ptr[device]) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    cudaFuncAttributes attr;
+    for (const void* f : {(const void*)ws_apply_noalloc_kernel<true>, (const void*)ws_apply_noalloc_kernel<false>}) {
+      if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, f);
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    }
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, (const void*)ws_noalloc_reduce_kernel);
     if (e != cudaSuccess) {
-      set_last_error((std::string("cudaGetSymbolAddress(no-alloc scratch): ") + cudaGetErrorString(e)).c_str());
+      set_last_error((std::string("no-alloc set-up: ") + cudaGetErrorString(e)).c_str());
       return WS_ERR_CUDA;
     }
     g_noalloc_ptr[device] = static_cast<ws_device_result*>(p);
@@ -918,7 +984,6 @@ static int ws_apply_device_noalloc_impl(const void* tiles, uint32_t ntiles, cons
   auto kernel = reverse ? ws_apply_noalloc_kernel<true> : ws_apply_noalloc_kernel<false>;
   // The slots used by this call start at zero; the array keeps the previous call's values otherwise.
   e = cudaMemsetAsync(scratch, 0, sizeof(ws_device_result) * ntiles, s);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
   if (e == cudaSuccess) {
     kernel<<<ntiles, kThreads, kSmemBytes, s>>>(static_cast<const ws_tile_desc*>(tiles),
                                                  static_cast<const ws_block_desc*>(blocks), tables,

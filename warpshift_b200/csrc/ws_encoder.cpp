@@ -189,17 +189,22 @@ void build_candidate(const uint8_t* base, const uint8_t* target, uint64_t n, con
       word_counts[v]++;
     }
   }
-  // Word dictionary candidates: the distinct words in increasing order.
-  std::vector<uint16_t> words;
-  std::vector<uint64_t> wcounts;
+  // Word dictionary candidates: the distinct words in increasing order, and the
+  // distinct values of their high 12 bits.
+  std::vector<uint16_t> words, high_words;
+  std::vector<uint64_t> wcounts, high_counts;
   for (uint32_t v = 0; v < 65536; ++v)
     if (word_counts[v]) {
       words.push_back((uint16_t)v);
       wcounts.push_back(word_counts[v]);
     }
+  split_words(words, wcounts, 4, &high_words, &high_counts);
   CodingTables ct;
-  choose_coding(counts, words, wcounts, words.size() > 255, coded_blocks, co, &ct);
+  choose_coding(counts, words, wcounts, words.size() > 255, high_words, high_counts, high_words.size() > 255,
+                coded_blocks, co, &ct);
   const bool use_dict = ct.dict;
+  const uint32_t k = ct.split;
+  const uint16_t keep = (uint16_t)~((1u << k) - 1u);  // the coded part of a word
   const uint8_t esc = (uint8_t)ct.words.size();  // the escape symbol (when ct.escape)
   std::vector<uint8_t> index_of;
   if (use_dict) {
@@ -213,10 +218,11 @@ void build_candidate(const uint8_t* base, const uint8_t* target, uint64_t n, con
   const uint32_t* freq[2] = {ct.freq[0], ct.freq[1]};
   const uint32_t* cdf[2] = {ct.cdf[0], ct.cdf[1]};
   std::vector<uint8_t> s0(WS_BLOCK_BYTES / 2), s1(WS_BLOCK_BYTES / 2);
-  for (uint32_t k = 0; k < nblk; ++k) {
-    if (!nonzero[k]) continue;
+  std::vector<uint16_t> vw(WS_BLOCK_BYTES / 2);
+  for (uint32_t b = 0; b < nblk; ++b) {
+    if (!nonzero[b]) continue;
     EncodedBlock blk;
-    blk.offset = k * WS_BLOCK_BYTES;
+    blk.offset = b * WS_BLOCK_BYTES;
     blk.nbytes = (uint32_t)std::min<uint64_t>(WS_BLOCK_BYTES, n - blk.offset);
     blk.tail = 0;
     blk.flags = 0;
@@ -226,10 +232,12 @@ void build_candidate(const uint8_t* base, const uint8_t* target, uint64_t n, con
     for (auto& l : lanes) l.clear();
     for (uint32_t w = 0; w < wb; ++w) {
       const uint16_t v = residual_word<U16>(bb, tb, w);
+      vw[w] = v;
       if (use_dict) {
-        s0[w] = s1[w] = index_of[v];
-        if (ct.escape && index_of[v] == esc)
-          lanes[(w % WS_GROUP_WORDS) / WS_WORDS_PER_LANE].push_back(w | ((uint32_t)v << 16));
+        const uint16_t h = (uint16_t)(v & keep);
+        s0[w] = s1[w] = index_of[h];
+        if (ct.escape && index_of[h] == esc)
+          lanes[(w % WS_GROUP_WORDS) / WS_WORDS_PER_LANE].push_back(w | ((uint32_t)h << 16));
       } else {
         s0[w] = (uint8_t)(v & 0xFF);
         s1[w] = (uint8_t)(v >> 8);
@@ -247,6 +255,10 @@ void build_candidate(const uint8_t* base, const uint8_t* target, uint64_t n, con
     const uint8_t* sym[2] = {s0.data(), s1.data()};
     encode_ans_block(sc, sym, wb, freq, cdf, &blk.payload, &blk.nwords);
     blk.kind = use_dict ? (U16 ? WS_KIND_DICT_U16 : WS_KIND_DICT_XOR) : (U16 ? WS_KIND_ANS_U16 : WS_KIND_ANS_XOR);
+    if (k) {
+      blk.flags |= (uint8_t)ws_split_flags(k);
+      append_split_raw(vw.data(), wb, k, &blk.payload);
+    }
     if (escaped) {
       blk.flags |= WS_FLAG_ESCAPES;
       append_escapes(lanes, &blk.payload);
@@ -365,9 +377,88 @@ double dict_tables(const std::vector<uint16_t>& words, const uint64_t* sym_count
 
 }  // namespace
 
+namespace {
+
+// The best dictionary of one symbol alphabet (distinct values `words`,
+// increasing, with `counts`): every value a symbol, or (escapes) the K most
+// frequent ones (ties: smaller value first) plus the escape symbol. Returns the
+// estimated payload bytes, with `raw_bytes` added for a split coding's raw
+// sections, and the number of kept symbols in *kept (words.size() when none is
+// escaped); with `out`, fills the tables.
+double best_dictionary(const std::vector<uint16_t>& words, const std::vector<uint64_t>& counts, double raw_bytes,
+                       uint32_t coded_blocks, const CodingOptions& co, size_t* kept, CodingTables* out) {
+  double best = dict_tables(words, counts.data(), false, 0, coded_blocks, nullptr) + raw_bytes;
+  size_t best_k = words.size();
+  std::vector<uint32_t> order(words.size());
+  std::iota(order.begin(), order.end(), 0u);
+  std::stable_sort(order.begin(), order.end(), [&](uint32_t x, uint32_t y) { return counts[x] > counts[y]; });
+  auto subset = [&](size_t k, std::vector<uint16_t>* kw, std::vector<uint64_t>* kc) {
+    uint64_t escaped = 0;
+    for (size_t r = k; r < order.size(); ++r) escaped += counts[order[r]];
+    std::vector<uint32_t> keep(order.begin(), order.begin() + k);
+    std::sort(keep.begin(), keep.end());
+    kw->clear();
+    kc->clear();
+    for (uint32_t i : keep) {
+      kw->push_back(words[i]);
+      kc->push_back(counts[i]);
+    }
+    kc->push_back(escaped);
+    return escaped;
+  };
+  if (co.escapes >= 0) {
+    const uint64_t total = std::accumulate(counts.begin(), counts.end(), (uint64_t)0);
+    bool first = true;
+    std::vector<uint16_t> kw;
+    std::vector<uint64_t> kc;
+    for (size_t k : {8, 12, 16, 24, 32, 48, 64, 96, 128, 192}) {
+      if (k >= words.size()) break;
+      const uint64_t escaped = subset(k, &kw, &kc);
+      if (escaped * 100 > total) continue;  // keep the per-lane lists short
+      const double est = dict_tables(kw, kc.data(), true, escaped, coded_blocks, nullptr) + raw_bytes;
+      if (est < best || (co.escapes > 0 && first)) {
+        best = est;
+        best_k = k;
+        first = false;
+      }
+    }
+  }
+  *kept = best_k;
+  if (out) {
+    if (best_k == words.size()) {
+      dict_tables(words, counts.data(), false, 0, coded_blocks, out);
+    } else {
+      std::vector<uint16_t> kw;
+      std::vector<uint64_t> kc;
+      const uint64_t escaped = subset(best_k, &kw, &kc);
+      dict_tables(kw, kc.data(), true, escaped, coded_blocks, out);
+    }
+  }
+  return best;
+}
+
+}  // namespace
+
+void split_words(const std::vector<uint16_t>& words, const std::vector<uint64_t>& counts, uint32_t k,
+                 std::vector<uint16_t>* out_words, std::vector<uint64_t>* out_counts) {
+  const uint16_t keep = (uint16_t)~((1u << k) - 1u);
+  out_words->clear();
+  out_counts->clear();
+  for (size_t i = 0; i < words.size(); ++i) {  // increasing words keep equal high parts adjacent
+    const uint16_t h = (uint16_t)(words[i] & keep);
+    if (!out_words->empty() && out_words->back() == h) {
+      out_counts->back() += counts[i];
+    } else {
+      out_words->push_back(h);
+      out_counts->push_back(counts[i]);
+    }
+  }
+}
+
 void choose_coding(const uint64_t counts[2][256], const std::vector<uint16_t>& words,
-                   const std::vector<uint64_t>& word_counts, bool many_words, uint32_t coded_blocks,
-                   const CodingOptions& co, CodingTables* out) {
+                   const std::vector<uint64_t>& word_counts, bool many_words,
+                   const std::vector<uint16_t>& high_words, const std::vector<uint64_t>& high_counts,
+                   bool many_high, uint32_t coded_blocks, const CodingOptions& co, CodingTables* out) {
   PlaneTables t;
   uint32_t plane_entries[512];
   tables_from_counts(counts, &t, plane_entries);
@@ -375,69 +466,71 @@ void choose_coding(const uint64_t counts[2][256], const std::vector<uint16_t>& w
                             estimate_bytes(counts[1], t.freq[1], 256, 0);
   out->dict = false;
   out->escape = false;
+  out->split = 0;
   out->words.clear();
-  if (co.dict_slack_pct >= 0 && !many_words && words.size() >= 2 && words.size() <= 255) {
-    // Plain dictionary: every distinct word is a symbol.
-    double best = dict_tables(words, word_counts.data(), false, 0, coded_blocks, nullptr);
-    size_t best_k = words.size();
-    // Dictionaries with escapes: the K most frequent words (ties: smaller word
-    // first) are symbols, every other word is escaped.
-    if (co.escapes >= 0) {
-      std::vector<uint32_t> order(words.size());
-      std::iota(order.begin(), order.end(), 0u);
-      std::stable_sort(order.begin(), order.end(),
-                       [&](uint32_t x, uint32_t y) { return word_counts[x] > word_counts[y]; });
-      const uint64_t total = std::accumulate(word_counts.begin(), word_counts.end(), (uint64_t)0);
-      bool first = true;
-      for (size_t k : {8, 12, 16, 24, 32, 48, 64, 96, 128, 192}) {
-        if (k >= words.size()) break;
-        uint64_t escaped = 0;
-        for (size_t r = k; r < order.size(); ++r) escaped += word_counts[order[r]];
-        if (escaped * 100 > total) continue;  // keep the per-lane lists short
-        std::vector<uint32_t> kept(order.begin(), order.begin() + k);
-        std::sort(kept.begin(), kept.end());
-        std::vector<uint16_t> kw;
-        std::vector<uint64_t> kc;
-        for (uint32_t i : kept) {
-          kw.push_back(words[i]);
-          kc.push_back(word_counts[i]);
-        }
-        kc.push_back(escaped);
-        const double est = dict_tables(kw, kc.data(), true, escaped, coded_blocks, nullptr);
-        if (est < best || (co.escapes > 0 && first)) {
-          best = est;
-          best_k = k;
-          first = false;
-        }
+  if (co.dict_slack_pct >= 0) {
+    // Candidate alphabets: k = 0 (the words), 1, 2 (derived from the words) and
+    // 4 (the high 12 bits, counted separately because the words may be too many).
+    double best = 0;
+    int best_k = -1;
+    size_t best_kept = 0;
+    std::vector<uint16_t> best_words;
+    std::vector<uint64_t> best_counts;
+    for (uint32_t k : {0u, 1u, 2u, 4u}) {
+      const bool allowed = co.split > 0 ? k == (uint32_t)co.split : (k == 0 || co.split == 0);
+      if (!allowed) continue;
+      std::vector<uint16_t> sw;
+      std::vector<uint64_t> sc;
+      if (k == 4 && !many_high) {
+        sw = high_words;
+        sc = high_counts;
+      } else if (k < 4 && !many_words) {
+        split_words(words, word_counts, k, &sw, &sc);
+      } else {
+        continue;
+      }
+      if (sw.size() < 2 || sw.size() > 255) continue;
+      const double raw_bytes = (double)coded_blocks * ws_split_raw_bytes(WS_BLOCK_BYTES / 2, k);
+      size_t kept;
+      const double est = best_dictionary(sw, sc, raw_bytes, coded_blocks, co, &kept, nullptr);
+      if (best_k < 0 || est < best) {
+        best = est;
+        best_k = (int)k;
+        best_kept = kept;
+        best_words = std::move(sw);
+        best_counts = std::move(sc);
       }
     }
-    if (best <= planes_est * (1.0 + co.dict_slack_pct / 100.0) || (co.escapes > 0 && best_k < words.size())) {
-      if (best_k == words.size()) {
-        dict_tables(words, word_counts.data(), false, 0, coded_blocks, out);
-      } else {
-        std::vector<uint32_t> order(words.size());
-        std::iota(order.begin(), order.end(), 0u);
-        std::stable_sort(order.begin(), order.end(),
-                         [&](uint32_t x, uint32_t y) { return word_counts[x] > word_counts[y]; });
-        uint64_t escaped = 0;
-        for (size_t r = best_k; r < order.size(); ++r) escaped += word_counts[order[r]];
-        std::vector<uint32_t> kept(order.begin(), order.begin() + best_k);
-        std::sort(kept.begin(), kept.end());
-        std::vector<uint16_t> kw;
-        std::vector<uint64_t> kc;
-        for (uint32_t i : kept) {
-          kw.push_back(words[i]);
-          kc.push_back(word_counts[i]);
-        }
-        kc.push_back(escaped);
-        dict_tables(kw, kc.data(), true, escaped, coded_blocks, out);
-      }
+    // A forced split, or forced escapes that escape something, take the dictionary
+    // whatever its estimate.
+    const bool forced = best_k >= 0 && (co.split > 0 || (co.escapes > 0 && best_kept < best_words.size()));
+    if (best_k >= 0 && (forced || best <= planes_est * (1.0 + co.dict_slack_pct / 100.0))) {
+      size_t kept;
+      best_dictionary(best_words, best_counts,
+                      (double)coded_blocks * ws_split_raw_bytes(WS_BLOCK_BYTES / 2, (uint32_t)best_k), coded_blocks,
+                      co, &kept, out);
+      out->split = (uint32_t)best_k;
       return;
     }
   }
   memcpy(out->entries, plane_entries, sizeof(out->entries));
   memcpy(out->freq, t.freq, sizeof(out->freq));
   memcpy(out->cdf, t.cdf, sizeof(out->cdf));
+}
+
+void append_split_raw(const uint16_t* v, uint32_t W, uint32_t k, std::vector<uint8_t>* payload) {
+  const uint32_t bytes = ws_split_raw_bytes(W, k);
+  if (!bytes) return;
+  std::vector<uint32_t> raw(bytes / 4, 0);
+  const uint32_t per = 4u / k, mask = (1u << k) - 1u;
+  for (uint32_t w = 0; w < W; ++w) {
+    const uint32_t g = w / WS_GROUP_WORDS, lane = (w % WS_GROUP_WORDS) / WS_WORDS_PER_LANE, j = w % WS_WORDS_PER_LANE;
+    const uint32_t bit = ((j & 1u) ? 16u : 0u) + (g % per) * 4u * k + (j >> 1) * k;
+    raw[(g / per) * WS_LANES + lane] |= ((uint32_t)v[w] & mask) << bit;
+  }
+  const size_t at = payload->size();
+  payload->resize(at + bytes);
+  memcpy(payload->data() + at, raw.data(), bytes);
 }
 
 void u16_residual_reference(const uint8_t* base, const uint8_t* target, uint64_t nbytes, uint8_t* out) {

@@ -34,29 +34,49 @@ struct EncodedPacket {
 struct CodingOptions {
   int dict_slack_pct = 6;  // word dictionary when within this many % of the byte planes' size; < 0: never
   int escapes = 0;         // dictionary with escapes: 0 when smaller, < 0 never, > 0 whenever eligible
+  int split = 0;           // split words: 0 the k (0, 1, 2, 4) estimated smallest, < 0 never,
+                           // 1, 2 or 4: that k whenever eligible (WS_FLAG_SPLIT_MASK)
 };
 
 // Tables of one packet coding: byte planes (two tables) or word dictionary
 // (one table for both states, whose symbols index `words`; with `escape`, the
 // extra symbol words.size() stands for every other word, decoded as word 0 and
-// listed per block after the stream, see WS_FLAG_ESCAPES).
+// listed per block after the stream, see WS_FLAG_ESCAPES). A split-word
+// dictionary (`split` = k > 0) codes each word with its low k bits cleared
+// (`words` have them clear) and stores those bits raw.
 struct CodingTables {
   bool dict = false;
   bool escape = false;
+  uint32_t split = 0;
   uint32_t entries[512];          // slot entries as the kernel reads them
   uint32_t freq[2][256], cdf[2][256];
   std::vector<uint16_t> words;    // dictionary: word of each kept symbol, increasing
 };
 
 // Builds the byte-plane tables from `counts` (plane histograms over the coded
-// words) and switches to the word dictionary when the packet has 2..255
-// distinct words (`words` increasing, `word_counts` aligned; many_words = more
-// than 255) and its estimated size is within dict_slack_pct % of the planes'.
-// The dictionary keeps all words, or (escapes) only the most frequent ones when
-// that is estimated smaller and the escaped words are at most 1 % of the words.
+// words) and switches to a word dictionary when one is estimated within
+// dict_slack_pct % of the planes' size. Dictionaries: of the words themselves
+// or, split, of the words with their low k bits cleared (k = 1, 2 from `words`;
+// k = 4 from `high_words`, the distinct values of word & 0xFFF0); each needs
+// 2..255 distinct values (`words` increasing, `word_counts` aligned, many_words
+// = more than 255 distinct words; likewise high_words / high_counts /
+// many_high). A dictionary keeps all its values, or (escapes) only the most
+// frequent ones when that is estimated smaller and the escaped words are at
+// most 1 % of the words. The smallest estimate wins (ties: smaller k).
 void choose_coding(const uint64_t counts[2][256], const std::vector<uint16_t>& words,
-                   const std::vector<uint64_t>& word_counts, bool many_words, uint32_t coded_blocks,
-                   const CodingOptions& co, CodingTables* out);
+                   const std::vector<uint64_t>& word_counts, bool many_words,
+                   const std::vector<uint16_t>& high_words, const std::vector<uint64_t>& high_counts,
+                   bool many_high, uint32_t coded_blocks, const CodingOptions& co, CodingTables* out);
+
+// Distinct values of (word & ~(2^k - 1)) with summed counts, increasing, from
+// the increasing distinct `words` and their counts.
+void split_words(const std::vector<uint16_t>& words, const std::vector<uint64_t>& counts, uint32_t k,
+                 std::vector<uint16_t>* out_words, std::vector<uint64_t>* out_counts);
+
+// Appends a split-word block's raw section (WS_FLAG_SPLIT_MASK layout) for its
+// residual words v[0..W) and k raw bits to a payload whose stream part is
+// padded to 16 bytes.
+void append_split_raw(const uint16_t* v, uint32_t W, uint32_t k, std::vector<uint8_t>* payload);
 
 // Quantise symbol counts to frequencies summing to WS_PROB_SCALE; every symbol
 // with a non-zero count gets frequency >= 1. Greedy fix-up minimising code length.

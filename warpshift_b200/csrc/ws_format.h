@@ -69,6 +69,21 @@ enum ws_kind {
 #define WS_FLAG_ESCAPES 2u
 #define WS_ESCAPE_LANE_MAX 64u  // entries per lane at most; an encoder codes a block with more as RAW
 #define WS_ESCAPE_HEADER_BYTES 64u
+// Split words (word-dictionary blocks only): flags bits 2-3 hold a code c and
+// the low k = {0, 1, 2, 4}[c] bits of every residual word are stored raw; the
+// dictionary codes the word with those bits cleared (its entries carry the
+// word with the low k bits zero, so decoding is unchanged). The raw section
+// follows the stream at byte align16(2 * nwords) and precedes any escape list;
+// it is read, not staged. It holds uint32 raw words: G = 4 / k groups share one
+// word per lane, raw word (g / G) * 32 + lane for group g; inside it group g
+// starts at bit o = (g % G) * 4k, and the lane's word pair j (words 2j, 2j+1 of
+// its 8) keeps word 2j's bits at [o + jk, o + jk + k) and word 2j+1's at
+// [16 + o + jk, 16 + o + jk + k), so one shift and one mask put a pair's bits
+// in place. Words past the block's end have zero bits. The section is
+// 4 * 32 * ceil(ceil(W / 256) / G) bytes (a multiple of 16). An escaped word's
+// list entry carries the word with its low k bits cleared.
+#define WS_FLAG_SPLIT_SHIFT 2u
+#define WS_FLAG_SPLIT_MASK 0x0Cu
 
 // Device-side errors reported through ws_device_result.errors.
 #define WS_DEVERR_STATE 1u     // final rANS state != WS_RANS_L
@@ -134,6 +149,21 @@ typedef struct ws_device_result {
 #else
 #define WS_HD static inline
 #endif
+
+// Raw low bits per word of a split-word block (0 when not split).
+WS_HD uint32_t ws_split_bits(uint32_t flags) {
+  const uint32_t c = (flags & WS_FLAG_SPLIT_MASK) >> WS_FLAG_SPLIT_SHIFT;
+  return c == 3u ? 4u : c;
+}
+// Flag bits of a split of k raw bits (k in {0, 1, 2, 4}).
+WS_HD uint32_t ws_split_flags(uint32_t k) { return (k == 4u ? 3u : k) << WS_FLAG_SPLIT_SHIFT; }
+// Bytes of a split-word block's raw section for W coded words and k raw bits.
+WS_HD uint32_t ws_split_raw_bytes(uint32_t W, uint32_t k) {
+  if (k == 0u) return 0u;
+  const uint32_t groups = (W + WS_GROUP_WORDS - 1u) / WS_GROUP_WORDS;
+  const uint32_t per = 4u / k;  // groups per raw word
+  return 4u * WS_LANES * ((groups + per - 1u) / per);
+}
 
 WS_HD uint64_t ws_mix64(uint64_t x) {
   x ^= x >> 30;

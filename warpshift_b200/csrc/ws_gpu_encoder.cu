@@ -17,6 +17,8 @@
 #include <stdint.h>
 #include <string.h>
 #include <sys/mman.h>
+#include <sys/syscall.h>
+#include <unistd.h>
 
 #include <stdio.h>
 #include <stdlib.h>
@@ -46,10 +48,11 @@ constexpr uint32_t kMaxDistinct = 255;
 
 struct PacketStats {  // device, one per packet of the batch
   uint32_t plane[2][2][256];  // [transform xor/u16][plane][symbol]
-  uint32_t key[2][kPacketSlots];  // word + 1, 0 = empty
-  uint32_t cnt[2][kPacketSlots];
-  uint32_t distinct[2];
-  uint32_t many[2];
+  // Distinct words ([0]) and distinct high 12 bits (word & 0xFFF0, [1]) per transform.
+  uint32_t key[2][2][kPacketSlots];  // [table][transform]: value + 1, 0 = empty
+  uint32_t cnt[2][2][kPacketSlots];
+  uint32_t distinct[2][2];
+  uint32_t many[2][2];
 };
 
 struct BlockStats {  // device, one per block of the batch
@@ -71,6 +74,7 @@ struct EncodeJob {  // one block coded with one candidate
   uint32_t dict;      // 1: word dictionary, 0: byte planes
   uint32_t u16;       // 1: U16 residual words, 0: XOR words
   uint32_t esc;       // the dictionary's escape symbol, or ~0u without escapes
+  uint32_t split;     // raw low bits per word of a split-word dictionary (0, 1, 2, 4)
 };
 
 struct EncTable {  // per candidate coding: per state, per symbol
@@ -84,6 +88,8 @@ struct CompactJob {
   uint32_t nwords;     // ANS halfwords incl. header
   uint32_t escapes;    // escape entries listed after the stream (0: no list)
   uint64_t dst;        // byte offset in the output buffer
+  uint32_t split;      // raw low bits per word (0: no raw section)
+  uint32_t u16;        // the raw bits are of U16 residual words
 };
 
 __device__ __forceinline__ uint16_t u16_word(uint16_t b, uint16_t t) {
@@ -145,18 +151,19 @@ __device__ bool table_add(uint32_t* key, uint32_t* cnt, uint32_t* distinct, uint
 __global__ void __launch_bounds__(kStatsThreads) stats_kernel(const BlockJob* __restrict__ jobs, PacketStats* pstats,
                                                               BlockStats* bstats) {
   __shared__ uint32_t hist[2][2][256];
-  __shared__ uint32_t key[2][kLocalSlots], cnt[2][kLocalSlots];
-  __shared__ uint32_t distinct[2], overflow[2];
+  // [table][transform]: table 0 counts words, table 1 their high 12 bits.
+  __shared__ uint32_t key[2][2][kLocalSlots], cnt[2][2][kLocalSlots];
+  __shared__ uint32_t distinct[2][2], overflow[2][2];
   __shared__ uint32_t ck[4][kStatsThreads];  // aB, bB, aA, bA per thread
   const uint32_t t = threadIdx.x;
   for (uint32_t i = t; i < 2 * 2 * 256; i += kStatsThreads) (&hist[0][0][0])[i] = 0;
-  for (uint32_t i = t; i < 2 * kLocalSlots; i += kStatsThreads) {
-    (&key[0][0])[i] = 0;
-    (&cnt[0][0])[i] = 0;
+  for (uint32_t i = t; i < 2 * 2 * kLocalSlots; i += kStatsThreads) {
+    (&key[0][0][0])[i] = 0;
+    (&cnt[0][0][0])[i] = 0;
   }
-  if (t < 2) {
-    distinct[t] = 0;
-    overflow[t] = 0;
+  if (t < 4) {
+    (&distinct[0][0])[t] = 0;
+    (&overflow[0][0])[t] = 0;
   }
   __syncthreads();
   const BlockJob job = jobs[blockIdx.x];
@@ -199,7 +206,9 @@ __global__ void __launch_bounds__(kStatsThreads) stats_kernel(const BlockJob* __
       for (int c = 0; c < 2; ++c) {
         atomicAdd(&hist[c][0][v[c] & 0xFF], 1u);
         atomicAdd(&hist[c][1][v[c] >> 8], 1u);
-        if (!overflow[c] && !table_add(key[c], cnt[c], &distinct[c], 9, v[c], 1)) overflow[c] = 1;
+        if (!overflow[0][c] && !table_add(key[0][c], cnt[0][c], &distinct[0][c], 9, v[c], 1)) overflow[0][c] = 1;
+        if (!overflow[1][c] && !table_add(key[1][c], cnt[1][c], &distinct[1][c], 9, v[c] & 0xFFF0u, 1))
+          overflow[1][c] = 1;
       }
     }
   }
@@ -237,17 +246,19 @@ __global__ void __launch_bounds__(kStatsThreads) stats_kernel(const BlockJob* __
     const uint32_t v = (&hist[0][0][0])[i];
     if (v) atomicAdd(&(&ps->plane[0][0][0])[i], v);
   }
-  for (uint32_t c = 0; c < 2; ++c) {
-    if (overflow[c]) {
-      if (t == 0) atomicExch(&ps->many[c], 1u);
-      continue;
+  for (uint32_t h = 0; h < 2; ++h)
+    for (uint32_t c = 0; c < 2; ++c) {
+      if (overflow[h][c]) {
+        if (t == 0) atomicExch(&ps->many[h][c], 1u);
+        continue;
+      }
+      for (uint32_t i = t; i < kLocalSlots; i += kStatsThreads) {
+        const uint32_t k = key[h][c][i];
+        if (k && !ps->many[h][c] &&
+            !table_add(ps->key[h][c], ps->cnt[h][c], &ps->distinct[h][c], 10, k - 1, cnt[h][c][i]))
+          atomicExch(&ps->many[h][c], 1u);
+      }
     }
-    for (uint32_t i = t; i < kLocalSlots; i += kStatsThreads) {
-      const uint32_t k = key[c][i];
-      if (k && !ps->many[c] && !table_add(ps->key[c], ps->cnt[c], &ps->distinct[c], 10, k - 1, cnt[c][i]))
-        atomicExch(&ps->many[c], 1u);
-    }
-  }
 }
 
 // Dictionary index table of a packet: word -> symbol.
@@ -295,6 +306,7 @@ __global__ void __launch_bounds__(kEncWarps * 32) encode_kernel(const BlockJob* 
   const bool aligned = (((uintptr_t)blk.base | (uintptr_t)blk.target) & 15u) == 0;
   uint32_t x[2] = {WS_RANS_L, WS_RANS_L};
   uint32_t cursor = kOutHalfwords;
+  const uint16_t keep = (uint16_t)~((1u << job.split) - 1u);  // the coded part of a split word
   if (job.esc != ~0u) {
     // Escape list of this lane: its words coded as the escape symbol, in
     // increasing word order (at most WS_ESCAPE_LANE_MAX stored; the count is exact).
@@ -304,11 +316,13 @@ __global__ void __launch_bounds__(kEncWarps * 32) encode_kernel(const BlockJob* 
       const uint32_t w0 = g * WS_GROUP_WORDS + lane * WS_WORDS_PER_LANE;
       uint16_t v[8];
       load_words(blk, w0, W, aligned, job.u16 != 0, v);
-      for (uint32_t q = 0; q < 8; ++q)
-        if (w0 + q < W && idx[v[q]] == job.esc) {
-          if (count < WS_ESCAPE_LANE_MAX) mine[count] = (w0 + q) | ((uint32_t)v[q] << 16);
+      for (uint32_t q = 0; q < 8; ++q) {
+        const uint16_t h = (uint16_t)(v[q] & keep);
+        if (w0 + q < W && idx[h] == job.esc) {
+          if (count < WS_ESCAPE_LANE_MAX) mine[count] = (w0 + q) | ((uint32_t)h << 16);
           ++count;
         }
+      }
     }
     side_count[(uint64_t)j * WS_LANES + lane] = count;
   }
@@ -333,8 +347,8 @@ __global__ void __launch_bounds__(kEncWarps * 32) encode_kernel(const BlockJob* 
         pa[p] = w0 + ja < W;
         pb[p] = w0 + jb < W;
         if (job.dict) {
-          sa[p] = pa[p] ? idx[v[ja]] : 0;
-          sb[p] = pb[p] ? idx[v[jb]] : 0;
+          sa[p] = pa[p] ? idx[v[ja] & keep] : 0;
+          sb[p] = pb[p] ? idx[v[jb] & keep] : 0;
         } else {
           sa[p] = p ? (v[ja] >> 8) : (v[ja] & 0xFFu);
           sb[p] = p ? (v[jb] >> 8) : (v[jb] & 0xFFu);
@@ -408,6 +422,28 @@ __global__ void compact_kernel(const CompactJob* __restrict__ jobs, const BlockJ
       v = src[first + (i - WS_HEADER_HALFWORDS)];
     d16[i] = v;
   }
+  uint32_t side_off = 2 * padded_hw;
+  if (job.split) {
+    // Raw section (WS_FLAG_SPLIT_MASK layout): one thread per raw word.
+    const uint32_t k = job.split, per = 4u / k, mask = (1u << k) - 1u;
+    const uint32_t W = blk.nbytes / 2, raw_bytes = ws_split_raw_bytes(W, k);
+    const bool aligned = (((uintptr_t)blk.base | (uintptr_t)blk.target) & 15u) == 0;
+    uint32_t* raw = reinterpret_cast<uint32_t*>(d + side_off);
+    for (uint32_t r = threadIdx.x; r < raw_bytes / 4; r += blockDim.x) {
+      const uint32_t lane = r % WS_LANES, q = r / WS_LANES;
+      uint32_t acc = 0;
+      for (uint32_t gg = 0; gg < per; ++gg) {
+        const uint32_t g = q * per + gg;
+        uint16_t v[8];
+        load_words(blk, g * WS_GROUP_WORDS + lane * WS_WORDS_PER_LANE, W, aligned, job.u16 != 0, v);
+#pragma unroll
+        for (uint32_t j = 0; j < 8; ++j)
+          acc |= ((uint32_t)v[j] & mask) << (((j & 1u) ? 16u : 0u) + gg * 4u * k + (j >> 1) * k);
+      }
+      raw[r] = acc;
+    }
+    side_off += raw_bytes;
+  }
   if (job.escapes == 0) return;
   // Escape list (WS_FLAG_ESCAPES layout): lane counts, entries by lane, zero padding.
   __shared__ uint32_t start[WS_LANES + 1];
@@ -417,7 +453,7 @@ __global__ void compact_kernel(const CompactJob* __restrict__ jobs, const BlockJ
     for (uint32_t l = 0; l < WS_LANES; ++l) start[l + 1] = start[l] + cnt[l];
   }
   __syncthreads();
-  uint8_t* side = d + 2 * padded_hw;
+  uint8_t* side = d + side_off;
   uint16_t* head = reinterpret_cast<uint16_t*>(side);
   if (threadIdx.x < WS_LANES) head[threadIdx.x] = (uint16_t)cnt[threadIdx.x];
   uint32_t* ent = reinterpret_cast<uint32_t*>(side + WS_ESCAPE_HEADER_BYTES);
@@ -614,6 +650,31 @@ struct BatchInput {
 
 }  // namespace
 
+int device_numa_node(int device) {
+  char bus[64] = {0};
+  if (cudaDeviceGetPCIBusId(bus, (int)sizeof(bus), device) != cudaSuccess) return -1;
+  unsigned domain = 0, b = 0, d = 0, f = 0;
+  if (sscanf(bus, "%x:%x:%x.%x", &domain, &b, &d, &f) != 4) return -1;
+  char path[128];
+  snprintf(path, sizeof(path), "/sys/bus/pci/devices/%04x:%02x:%02x.%x/numa_node", domain, b, d, f);
+  FILE* fp = fopen(path, "r");
+  if (!fp) return -1;
+  int node = -1;
+  if (fscanf(fp, "%d", &node) != 1) node = -1;
+  fclose(fp);
+  return node;
+}
+
+bool prefer_numa_node(void* p, uint64_t size, int node) {
+  constexpr int kMaxNodes = 1024;
+  constexpr int kBits = 8 * (int)sizeof(unsigned long);
+  if (node < 0 || node >= kMaxNodes) return false;
+  unsigned long mask[kMaxNodes / kBits] = {0};
+  mask[node / kBits] = 1ul << (node % kBits);
+  const long kMpolPreferred = 1;  // pages go to `node` while it has free memory, elsewhere otherwise
+  return syscall(SYS_mbind, p, (unsigned long)size, kMpolPreferred, mask, (unsigned long)kMaxNodes, 0ul) == 0;
+}
+
 bool alloc_host_chunk(uint64_t bytes, bool pinned, int threads, ArenaChunk* out, std::string* err) {
   constexpr uint64_t kHuge = 2ull << 20;
   const uint64_t size = (std::max<uint64_t>(bytes, 1) + kHuge - 1) & ~(kHuge - 1);
@@ -625,6 +686,13 @@ bool alloc_host_chunk(uint64_t bytes, bool pinned, int threads, ArenaChunk* out,
   *out = ArenaChunk{(uint8_t*)p, 0, bytes, false};
   if (!pinned) return true;
   madvise(p, size, MADV_HUGEPAGE);  // advisory: fewer, larger pages to fault and lock
+  // The copy engines read the arena on every switch: place its pages on the
+  // NUMA node of the device's PCIe link (advisory; WS_ARENA_NUMA=0 leaves the
+  // placement to first touch).
+  const char* numa = getenv("WS_ARENA_NUMA");
+  int device = 0;
+  if (!(numa && numa[0] == '0') && cudaGetDevice(&device) == cudaSuccess)
+    prefer_numa_node(p, size, device_numa_node(device));
   const int nt = (int)std::max<uint64_t>(1, std::min<uint64_t>((uint64_t)std::max(1, std::min(threads, 8)), size / (8ull << 20)));
   const uint64_t per = (size / nt + kHuge - 1) & ~(kHuge - 1);
   std::vector<std::thread> pool;
@@ -811,20 +879,25 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
         uint64_t counts[2][256];
         for (int q = 0; q < 2; ++q)
           for (int s = 0; s < 256; ++s) counts[q][s] = ps.plane[c][q][s];
-        std::vector<std::pair<uint16_t, uint64_t>> wl;
-        const bool many = ps.many[c] != 0;
-        if (!many)
-          for (uint32_t k = 0; k < kPacketSlots; ++k)
-            if (ps.key[c][k]) wl.emplace_back((uint16_t)(ps.key[c][k] - 1), ps.cnt[c][k]);
-        std::sort(wl.begin(), wl.end());
-        std::vector<uint16_t> words;
-        std::vector<uint64_t> wcounts;
-        for (auto& pr : wl) {
-          words.push_back(pr.first);
-          wcounts.push_back(pr.second);
+        // Distinct words (h = 0) and distinct high 12 bits (h = 1), increasing.
+        std::vector<uint16_t> words[2];
+        std::vector<uint64_t> wcounts[2];
+        bool many[2];
+        for (int h = 0; h < 2; ++h) {
+          std::vector<std::pair<uint16_t, uint64_t>> wl;
+          many[h] = ps.many[h][c] != 0;
+          if (!many[h])
+            for (uint32_t k = 0; k < kPacketSlots; ++k)
+              if (ps.key[h][c][k]) wl.emplace_back((uint16_t)(ps.key[h][c][k] - 1), ps.cnt[h][c][k]);
+          std::sort(wl.begin(), wl.end());
+          for (auto& pr : wl) {
+            words[h].push_back(pr.first);
+            wcounts[h].push_back(pr.second);
+          }
         }
         CodingTables& ct = coding[2 * i + c];
-        choose_coding(counts, words, wcounts, many || words.size() > 255, coded, co, &ct);
+        choose_coding(counts, words[0], wcounts[0], many[0] || words[0].size() > 255, words[1], wcounts[1],
+                      many[1] || words[1].size() > 255, coded, co, &ct);
         Cand& cd = cand[2 * i + c];
         cd.table = (int)tables.size();
         cd.dict = ct.dict;
@@ -841,7 +914,7 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
         for (uint32_t b = packet_first_block[i]; b < packet_first_block[i + 1]; ++b) {
           if (!bstats[b].nonzero) continue;
           job_of[2 * i + c].push_back((uint32_t)jobs.size());
-          jobs.push_back(EncodeJob{b, (uint32_t)cd.table, ct.dict ? 1u : 0u, (uint32_t)c, esc});
+          jobs.push_back(EncodeJob{b, (uint32_t)cd.table, ct.dict ? 1u : 0u, (uint32_t)c, esc, ct.dict ? ct.split : 0u});
         }
       }
     }
@@ -854,6 +927,7 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
     // lane has more escapes than a list holds (the block is then coded raw).
     auto coded_size = [&](uint32_t jj, bool* ok, uint32_t* escapes) {
       uint32_t size = (2 * nwords[jj] + 15) & ~15u, total = 0, most = 0;
+      size += ws_split_raw_bytes(blocks[jobs[jj].block].nbytes / 2, jobs[jj].split);
       if (jobs[jj].esc != ~0u)
         for (uint32_t l = 0; l < WS_LANES; ++l) {
           total += side_count[(size_t)jj * WS_LANES + l];
@@ -948,7 +1022,7 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
         blk.lane_sum[0] = bstats[b].lane_sum[0];
         blk.lane_sum[1] = bstats[b].lane_sum[1];
         const uint32_t raw = (blk.nbytes + 15) & ~15u;
-        CompactJob cj{b, ~0u, 0, 0, out_bytes};
+        CompactJob cj{b, ~0u, 0, 0, out_bytes, 0, 0};
         uint32_t size = raw;
         if (best_c >= 0) {
           const uint32_t jj = job_of[2 * i + best_c][jpos];
@@ -965,9 +1039,12 @@ bool gpu_encode_packets(const std::vector<GpuPacketInput>& packets, int policy, 
               blk.tail = (uint8_t)bstats[b].tail;
             }
             if (esc_n) blk.flags |= WS_FLAG_ESCAPES;
+            blk.flags |= (uint8_t)ws_split_flags(jobs[jj].split);
             cj.encode = jj;
             cj.nwords = nwords[jj];
             cj.escapes = esc_n;
+            cj.split = jobs[jj].split;
+            cj.u16 = jobs[jj].u16;
             size = ans;
           }
         }

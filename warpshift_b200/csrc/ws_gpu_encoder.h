@@ -26,10 +26,19 @@ struct ArenaChunk {
   bool pinned;
 };
 
+// NUMA node that `device`'s PCIe link attaches to (sysfs numa_node), or -1
+// when the host reports none.
+int device_numa_node(int device);
+// Asks the kernel to place the pages of [p, p + size) on `node` while it has
+// free memory (mbind MPOL_PREFERRED, before the pages are first touched).
+// Advisory: returns false, changing nothing, when the host refuses.
+bool prefer_numa_node(void* p, uint64_t size, int node);
+
 // Allocates `bytes` of host memory for an arena chunk; with `pinned` it is
-// page-locked (transparent huge pages, first touch on up to `threads` threads,
-// then cudaHostRegister: about ten times faster than cudaHostAlloc's 4 KiB page
-// faults). Returns false with *err set.
+// page-locked (transparent huge pages, placed on the current device's NUMA
+// node, first touch on up to `threads` threads, then cudaHostRegister: about
+// ten times faster than cudaHostAlloc's 4 KiB page faults). Returns false
+// with *err set.
 bool alloc_host_chunk(uint64_t bytes, bool pinned, int threads, ArenaChunk* out, std::string* err);
 void free_host_chunk(const ArenaChunk& chunk);
 

@@ -149,6 +149,11 @@ std::string check_descriptors(const ws_plan* p) {
     } else if (d.kind <= WS_KIND_DICT_U16) {
       if (d.nwords < WS_HEADER_HALFWORDS || 2ull * d.nwords > d.clen)
         return "coded block " + std::to_string(k) + " has a bad stream length";
+      const uint32_t split = ws_split_bits(d.flags);
+      if (split && d.kind != WS_KIND_DICT_XOR && d.kind != WS_KIND_DICT_U16)
+        return "block " + std::to_string(k) + " splits words but is not a word-dictionary block";
+      if (split && ((2ull * d.nwords + 15u) & ~15ull) + ws_split_raw_bytes(d.nbytes / 2, split) > d.clen)
+        return "coded block " + std::to_string(k) + " has a raw section outside its payload";
     } else {
       return "block " + std::to_string(k) + " has an unknown kind";
     }

@@ -65,6 +65,7 @@ ws::CodingOptions coding_options(const ws_build_options& o) {
   ws::CodingOptions co;
   co.dict_slack_pct = o.dict_slack_pct;
   co.escapes = o.escapes;
+  co.split = o.split;
   return co;
 }
 

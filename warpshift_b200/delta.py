@@ -88,6 +88,8 @@ class DeltaWeights:
     the byte planes' size; negative = never), ``encode_on_device`` (prepare on
     the GPU), ``encode_batch_bytes`` (GPU encoder batch; 0 = 512 MiB),
     ``escapes`` (dictionaries with escape lists: 0 when smaller, -1 never, 1
+    whenever eligible), ``split`` (split-word dictionaries, whose words' low k
+    bits are stored raw: 0 the k estimated smallest, -1 never, 1 / 2 / 4 that k
     whenever eligible) and ``host_fallback`` (when the GPU encoder cannot get
     its device buffers, encode on host threads instead of raising
     RuntimeError; off by default). ``save`` / ``load`` persist a package
@@ -107,6 +109,7 @@ class DeltaWeights:
         encode_on_device: bool = True,
         encode_batch_bytes: int = 0,
         escapes: int = 0,
+        split: int = 0,
         host_fallback: bool = False,
     ) -> None:
         started = time.perf_counter()
@@ -141,6 +144,7 @@ class DeltaWeights:
             encode_batch_bytes=encode_batch_bytes,
             escapes=escapes,
             host_fallback=int(bool(host_fallback)),
+            split=split,
         )
         plan = ctypes.c_void_p()
         with torch.cuda.device(self.device):
