@@ -25,7 +25,7 @@ BLOCK_DTYPE = np.dtype(
         ("flags", "u1"),
     ]
 )
-TILE_DTYPE = np.dtype([("first_block", "<u4"), ("nblocks", "<u4"), ("table", "<u4"), ("pad", "<u4")])
+TILE_DTYPE = np.dtype([("first_block", "<u4"), ("nblocks", "<u4"), ("table", "<u4"), ("split", "<u4")])
 assert BLOCK_DTYPE.itemsize == 32 and TILE_DTYPE.itemsize == 16
 
 

@@ -38,8 +38,8 @@
  * k = 1, 2, 4 (c = 1, 2, 3) bits are not in the stream but in a raw section at
  * byte (2 * nwords + 15) & ~15 (escape lists, if any, move behind it). With
  * G = 4 / k groups per uint32, group g's bits for lane l are in uint32
- * (g / G) * 32 + l, starting at bit (g % G) * 4k; the lane's word j sits at
- * bit (j odd ? 16 : 0) + (j / 2) * k from there. The section has
+ * (g / G) * 32 + l, starting at bit (g % G) * 8k; the lane's word j sits at
+ * bit j * k from there. The section has
  * ceil(ceil(W / 256) / G) * 128 bytes. The residual word is the decoded (or
  * listed) word ORed with its raw bits.
  */
@@ -62,7 +62,7 @@ typedef struct {
 } o_block;
 
 typedef struct {
-  uint32_t first_block, nblocks, table, pad;
+  uint32_t first_block, nblocks, table, split;
 } o_tile;
 
 enum { O_RAW = 0, O_ANS_XOR = 1, O_ANS_U16 = 2, O_DICT_XOR = 3, O_DICT_U16 = 4 };
@@ -190,7 +190,7 @@ int wso_apply_block(const o_block* b, const uint8_t* payload, const uint32_t* ta
     for (uint32_t i = 0; i < W; ++i) {
       const uint32_t g = i / 256u, l = (i % 256u) / 8u, j = i % 8u;
       const uint32_t rw = rd32(payload + side + 4u * ((g / per) * 32u + l));
-      const uint32_t bit = ((j & 1u) ? 16u : 0u) + (g % per) * 4u * k + (j / 2u) * k;
+      const uint32_t bit = (g % per) * 8u * k + j * k;
       raw_low[i] = (uint16_t)((rw >> bit) & ((1u << k) - 1u));
     }
     side += (uint32_t)raw_bytes;

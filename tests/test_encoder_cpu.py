@@ -305,29 +305,34 @@ def test_dictionary_needs_few_distinct_words_and_planes_cover_the_rest() -> None
 
 def test_split_words_shrink_the_stream_where_low_bits_are_noise() -> None:
     """Split-word dictionaries (the low k bits of each word stored raw, the rest
-    coded) are chosen when estimated smaller: XOR s = 0.01 codes with k = 1,
-    XOR s = 0.1 moves from byte planes to a k = 4 dictionary, U16 s = 0.1 takes
-    k = 4; every plan decodes exactly through the oracle."""
-    cases = [("xor", 0.01, 1, 0.99), ("xor", 0.1, 4, 0.90), ("u16", 0.1, 4, 0.985)]
-    for policy, scale, k, bound in cases:
+    coded): XOR s = 0.1 moves from byte planes to a k = 4 dictionary by default
+    (13 % smaller); XOR s = 0.01 with k = 1 and U16 s = 0.1 with k = 4 are
+    smaller too, but by less than the 3 % a split must save over the whole-word
+    dictionary, so the default keeps whole words there. Every plan decodes
+    exactly through the oracle."""
+    # (policy, scale, k, its size bound against split = -1, the k the default picks)
+    cases = [("xor", 0.01, 1, 0.99, 0), ("xor", 0.1, 4, 0.90, 4), ("u16", 0.1, 4, 0.985, 0)]
+    for policy, scale, k, bound, default_k in cases:
         a_t, b_t = bf16_pair(1 << 20, scale, 21)
         sizes = {}
-        for split in (-1, 0):
+        for split in (-1, 0, k):
             work = {"w": b_t.clone()}
             plan = host_plan({"w": a_t}, work, policy, split=split)
             try:
                 blocks, tiles, tables, arena, stats = plan_arrays(plan)
                 sizes[split] = int(stats.arena_bytes)
                 coded = blocks[blocks["kind"] != KIND_RAW]
-                assert {split_bits(f) for f in coded["flags"]} == ({0} if split < 0 else {k}), (policy, scale)
-                if split == 0:
+                want = {0: default_k, -1: 0}.get(split, k)
+                assert {split_bits(f) for f in coded["flags"]} == {want}, (policy, scale, split)
+                assert set(tiles["split"][tiles["table"] != 0xFFFFFFFF]) == {(0, 1, 2, 3, 3)[want]}
+                if want:
                     assert set(coded["kind"]) <= {KIND_DICT_XOR, KIND_DICT_U16}
                 err, ck = ostream.apply_plan(blocks, tiles, tables, arena, 0, True, 2)
                 assert err == 0 and ck == stats.expected_checksum[1]
                 np.testing.assert_array_equal(as_bytes(work["w"]), as_bytes(a_t))
             finally:
                 _lib.load().ws_plan_destroy(plan)
-        assert sizes[0] < sizes[-1] * bound, (policy, scale, sizes)
+        assert sizes[k] < sizes[-1] * bound, (policy, scale, sizes)
 
 
 def residual_words(a_t: torch.Tensor, b_t: torch.Tensor, policy: str) -> np.ndarray:
@@ -344,9 +349,9 @@ def residual_words(a_t: torch.Tensor, b_t: torch.Tensor, policy: str) -> np.ndar
 @pytest.mark.parametrize("policy", ["xor", "u16"])
 def test_split_raw_section_holds_each_words_low_bits(policy: str, k: int) -> None:
     """The raw section of every split block, read back by the layout's own rule
-    (raw word (g / G) * 32 + lane, G = 4 / k, bit (g % G) * 4k + (j odd) * 16 +
-    (j / 2) * k), equals the low k bits of the reference residual words; a
-    flipped raw bit changes exactly that word of the applied result."""
+    (raw word (g / G) * 32 + lane, G = 4 / k, bit (g % G) * 8k + j * k), equals
+    the low k bits of the reference residual words; a flipped raw bit changes
+    exactly that word of the applied result."""
     a_t, b_t = bf16_pair(70001, 0.01, 22)  # a partial last group and block
     work = {"w": b_t.clone()}
     plan = host_plan({"w": a_t}, work, policy, dict_slack_pct=100, split=k)
@@ -365,16 +370,16 @@ def test_split_raw_section_holds_each_words_low_bits(policy: str, k: int) -> Non
             raw = arena[off: off + split_raw_bytes(W, k)].view(np.uint32)
             w = np.arange(W)
             g, lane, j = w // 256, (w % 256) // 8, w % 8
-            bit = (j & 1) * 16 + (g % per) * 4 * k + (j // 2) * k
+            bit = (g % per) * 8 * k + j * k
             got = (raw[(g // per) * 32 + lane] >> bit.astype(np.uint32)) & mask
             np.testing.assert_array_equal(got, r[first: first + W] & mask)
             checked += 1
         assert checked >= 1
         blk = next(bk for bk in blocks if bk["kind"] != KIND_RAW)
         off = int(blk["src"]) + ((2 * int(blk["nwords"]) + 15) & ~15)
-        word = 256 * 3 + 8 * 7 + 5  # group 3, lane 7, lane word 5 (odd: high half)
+        word = 256 * 3 + 8 * 7 + 5  # group 3, lane 7, lane word 5
         g, lane, j = 3, 7, 5
-        bit = 16 + (g % per) * 4 * k + (j // 2) * k
+        bit = (g % per) * 8 * k + j * k
         raw = arena[off: off + split_raw_bytes(int(blk["nbytes"]) // 2, k)].view(np.uint32)
         raw[(g // per) * 32 + lane] ^= np.uint32(1 << bit)
         err, ck = ostream.apply_plan(blocks, tiles, tables, arena, 0, True, 2)

@@ -200,24 +200,24 @@ def test_gpu_encoder_under_memory_pressure(cuda_device, leave_mb: int, encoder: 
         lib.ws_plan_destroy(p_host)
 
 
-@pytest.mark.parametrize("policy, scale, ks", [("xor", 0.01, {1}), ("xor", 0.1, {4}), ("u16", 0.1, {2, 4})])
-def test_split_words_on_teacher_like_residuals(cuda_device, policy: str, scale: float, ks: set) -> None:
-    """The default coding of relative-noise BF16 pairs splits words (k = 1 at
-    XOR s = 0.01, k = 4 at XOR s = 0.1; U16 s = 0.1 estimates k = 2 and k = 4
-    within 0.1 % of each other): both encoders give the same plan, and the
+@pytest.mark.parametrize("policy, scale, split, ks", [("xor", 0.01, 1, {1}), ("xor", 0.1, 0, {4}), ("u16", 0.1, 2, {2}),
+                                                     ("u16", 0.1, 4, {4})])
+def test_split_words_on_teacher_like_residuals(cuda_device, policy: str, scale: float, split: int, ks: set) -> None:
+    """Split words on relative-noise BF16 pairs (the default picks k = 4 at XOR
+    s = 0.1; the others are forced): both encoders give the same plan, and the
     kernel switches B -> A -> B exactly."""
     from tests.helpers import split_bits
 
     x, y = bf16_pair((24 << 20) // 2 + 4097, scale, 41)  # two packets, partial last block and group
     b_dev = {"w": y.to(cuda_device)}
     lib = _lib.load()
-    p_gpu = build({"w": x}, b_dev, policy, 6, True, pin_arena=1)
-    p_host = build({"w": x}, b_dev, policy, 6, False)
+    p_gpu = build({"w": x}, b_dev, policy, 6, True, pin_arena=1, split=split)
+    p_host = build({"w": x}, b_dev, policy, 6, False, split=split)
     try:
         assert_same_plan(p_gpu, p_host)
         blocks = plan_arrays(p_gpu)[0]
         coded = blocks[blocks["kind"] != 0]
-        assert {split_bits(f) for f in coded["flags"]} <= ks
+        assert {split_bits(f) for f in coded["flags"]} == ks
         stream = torch.cuda.current_stream().cuda_stream
         _lib.check(lib.ws_plan_upload(p_gpu, stream))
         res = _lib.ApplyResult()

@@ -195,8 +195,15 @@ def test_descriptors_that_could_reach_outside_the_buffers_are_rejected(saved, tm
         k = first_coded(bl)
         bl["nwords"][k] = bl["clen"][k]  # 2 * nwords bytes no longer fit the payload
 
+    def tile_split(bl, ti):  # a split code the kernel has no expansion table for
+        ti["split"][0] = 5
+
+    def block_split(bl, ti):  # a block whose split code is not its tile's
+        bl["flags"][int(ti["first_block"][0])] ^= 3 << 2
+
     cases = {outside: "writes outside its tensor", shift16: "not a multiple of 16", kind: "unknown kind",
-             table: "bad table", stream_length: "bad stream length"}
+             table: "bad table", stream_length: "bad stream length", tile_split: "another split code",
+             block_split: "another split code|not a word-dictionary block|raw section outside"}
     for edit, message in cases.items():
         bad.write_bytes(rehashed(raw, edit))
         with pytest.raises(ValueError, match=message):

@@ -30,7 +30,7 @@ from warpshift_b200.delta import DeltaWeights
 pytestmark = pytest.mark.gpu
 
 
-def build_device_plan(a, targets, device):
+def build_device_plan(a, targets, device, policy: str = "auto", split: int = 0):
     """Host-side plan for `targets` (device tensors), its arrays copied into caller-owned torch memory."""
     lib = _lib.load()
     descs = (_lib.TensorDesc * len(a))()
@@ -38,8 +38,8 @@ def build_device_plan(a, targets, device):
         t = targets[name]
         descs[i] = _lib.TensorDesc(a[name].data_ptr(), t.data_ptr(), t.numel() * t.element_size(),
                                    int(t.dtype == torch.bfloat16), 0)
-    opts = _lib.BuildOptions(policy=_lib.POLICIES["auto"], threads=0, target_on_device=1, device=device.index,
-                             batch_bytes=0, staging_slots=0, pin_arena=0)
+    opts = _lib.BuildOptions(policy=_lib.POLICIES[policy], threads=0, target_on_device=1, device=device.index,
+                             batch_bytes=0, staging_slots=0, pin_arena=0, split=split)
     plan = ctypes.c_void_p()
     stream = torch.cuda.current_stream(device).cuda_stream
     _lib.check(lib.ws_plan_build(descs, len(a), ctypes.byref(opts), stream, ctypes.byref(plan)))
@@ -162,3 +162,30 @@ def test_noalloc_refuses_descriptors_outside_the_arrays(cuda_device, field: str)
         owner = max((n for n in bases if bases[n] <= dst), key=lambda n: bases[n])
         off, n = dst - bases[owner], int(dev["host_blocks"][i]["nbytes"])
         np.testing.assert_array_equal(as_bytes(targets[owner])[off : off + n], before[owner][off : off + n])
+
+
+@pytest.mark.parametrize("split", [2, 7])
+def test_noalloc_refuses_a_tile_split_code_its_blocks_do_not_have(cuda_device, split: int) -> None:
+    """A tile's split code names the raw-bit table its split-word blocks are
+    expanded with: blocks of another code are reported as WS_DEVERR_KIND and a
+    code that is not one of 0..3 refuses the tile (WS_DEVERR_BOUNDS); neither
+    writes the weights."""
+    from tests.helpers import bf16_pair, split_bits
+
+    x, y = bf16_pair(3 << 20, 0.01, 24)  # XOR s = 0.01: split words, k = 1
+    targets = {"w": y.to(cuda_device)}
+    dev = build_device_plan({"w": x}, targets, cuda_device, policy="xor", split=1)
+    tiles = dev["host_tiles"].copy()
+    victim = next(i for i, t in enumerate(tiles) if t["split"] == 1)
+    first, count = int(tiles[victim]["first_block"]), int(tiles[victim]["nblocks"])
+    assert all(split_bits(dev["host_blocks"][i]["flags"]) == 1 for i in range(first, first + count))
+    tiles[victim]["split"] = split
+    dev["tiles"] = torch.from_numpy(tiles.view(np.uint8).copy()).to(cuda_device)
+    before = as_bytes(targets["w"]).copy()
+    rc, result = call_noalloc(dev, True, cuda_device, check=False)
+    assert rc == _lib.WS_ERR_DEVICE
+    assert result.device_errors & (_lib.WS_DEVERR_BOUNDS if split > 3 else 8)
+    base = targets["w"].data_ptr()
+    for i in range(first, first + count):
+        off, n = int(dev["host_blocks"][i]["dst"]) - base, int(dev["host_blocks"][i]["nbytes"])
+        np.testing.assert_array_equal(as_bytes(targets["w"])[off : off + n], before[off : off + n])

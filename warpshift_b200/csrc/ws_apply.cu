@@ -46,7 +46,11 @@ constexpr uint32_t kFixedTableBase = 0x400;
 constexpr uint32_t kMirror = 640;  // a group reads <= 512 + 128 bytes past its start position
 constexpr uint32_t kRingStride = WS_RING_BYTES + kMirror;
 constexpr uint32_t kBarOffset = kRingOffset + kWarps * kRingStride;
-constexpr uint32_t kSmemBytes = kBarOffset + kWarps * 2 * 8;
+// Raw-bit expansion table of a tile whose packet splits words: entry b spreads
+// raw byte b over the word pairs it covers (16, 8 or 4 bytes for k = 1, 2, 4).
+constexpr uint32_t kSplitTabOffset = kBarOffset + kWarps * 2 * 8;
+constexpr uint32_t kSplitTabBytes = 256 * 16;
+constexpr uint32_t kSmemBytes = kSplitTabOffset + kSplitTabBytes;
 constexpr uint32_t kRingHalfwords = WS_RING_BYTES / 2;      // 1024
 constexpr uint32_t kHalfHalfwords = WS_RING_HALF_BYTES / 2; // 512
 constexpr uint32_t kWaitLimit = 1u << 20;      // bounded spin on a staging barrier
@@ -441,33 +445,65 @@ struct EscapeCursor {
   }
 };
 
-// Split-word blocks (SPLIT, dictionary kinds only): the low k bits of each
-// word come from the raw section after the stream (WS_FLAG_SPLIT_MASK layout in
-// ws_format.h), read with plain cached loads: one uint32 per lane covers 4 / k
-// groups, and one shift and mask per word pair put its bits in place.
+// Split-word blocks (K = 1, 2, 4 raw bits per word; dictionary kinds only): the
+// low bits of each word come from the raw section after the stream
+// (WS_FLAG_SPLIT_MASK layout in ws_format.h), read with plain cached loads. One
+// uint32 per lane covers 4 / K groups; a group's raw bits are K whole bytes, and
+// each byte is expanded through the tile's 256-entry table into the bits of the
+// word pairs it covers, so a group costs K byte selects (PRMT) and K shared
+// loads, and the bits join the residual in the apply's existing XOR.
+template <uint32_t K>
 struct SplitRaw {
   uint32_t off = 0;  // byte offset of the lane's first raw word in the payload
-  uint32_t k = 0;    // raw bits per word
 
-  // The raw word holding group g's bits and the bit offset of group g in it.
+  // The raw word holding group g's bits.
   __device__ __forceinline__ uint32_t load(const uint8_t* __restrict__ src, uint32_t g) const {
-    return __ldg(reinterpret_cast<const uint32_t*>(src + off) + ((g * k) >> 2) * WS_LANES);
+    return __ldg(reinterpret_cast<const uint32_t*>(src + off) + ((g * K) >> 2) * WS_LANES);
   }
-  __device__ __forceinline__ uint32_t offset(uint32_t g) const { return ((g * k) & 3u) << 2; }
-  __device__ __forceinline__ void merge(uint32_t rw, uint32_t o, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                        uint32_t& r3) const {
-    const uint32_t mask2 = (0x00010001u << k) - 0x00010001u;  // k low bits of both 16-bit halves
-    r0 |= (rw >> o) & mask2;
-    r1 |= (rw >> (o + k)) & mask2;
-    r2 |= (rw >> (o + 2u * k)) & mask2;
-    r3 |= (rw >> (o + 3u * k)) & mask2;
+  // The raw-bit contributions e0..e3 to the lane's word pairs of group g.
+  __device__ __forceinline__ void bits(uint32_t rw, uint32_t g, uint32_t& e0, uint32_t& e1, uint32_t& e2,
+                                       uint32_t& e3) const {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const uint8_t* tab = smem + kSplitTabOffset;
+    if (K == 1) {
+      const uint32_t b = prmt(rw, 0, 0x4440u | (g & 3u));
+      const uint4 e = reinterpret_cast<const uint4*>(tab)[b];
+      e0 = e.x, e1 = e.y, e2 = e.z, e3 = e.w;
+    } else if (K == 2) {
+      const uint32_t c = (g & 1u) * 2u;
+      const uint2 lo = reinterpret_cast<const uint2*>(tab)[prmt(rw, 0, 0x4440u | c)];
+      const uint2 hi = reinterpret_cast<const uint2*>(tab)[prmt(rw, 0, 0x4440u | (c + 1u))];
+      e0 = lo.x, e1 = lo.y, e2 = hi.x, e3 = hi.y;
+    } else {
+      const uint32_t* t = reinterpret_cast<const uint32_t*>(tab);
+      e0 = t[prmt(rw, 0, 0x4440u)];
+      e1 = t[prmt(rw, 0, 0x4441u)];
+      e2 = t[prmt(rw, 0, 0x4442u)];
+      e3 = t[prmt(rw, 0, 0x4443u)];
+    }
   }
 };
 
-template <bool U16, bool REVERSE, bool DICT, bool FIXED_BASE, bool SPLIT = false>
+// Thread t < 256 writes entry t of the expansion table for K raw bits per word.
+__device__ __forceinline__ void build_split_table(uint32_t k, uint32_t t) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* tab = smem + kSplitTabOffset;
+  auto pair = [&](uint32_t lo, uint32_t hi) { return lo | (hi << 16); };
+  if (k == 1) {
+    reinterpret_cast<uint4*>(tab)[t] = make_uint4(pair(t & 1u, (t >> 1) & 1u), pair((t >> 2) & 1u, (t >> 3) & 1u),
+                                                  pair((t >> 4) & 1u, (t >> 5) & 1u), pair((t >> 6) & 1u, t >> 7));
+  } else if (k == 2) {
+    reinterpret_cast<uint2*>(tab)[t] = make_uint2(pair(t & 3u, (t >> 2) & 3u), pair((t >> 4) & 3u, t >> 6));
+  } else {
+    reinterpret_cast<uint32_t*>(tab)[t] = pair(t & 15u, t >> 4);
+  }
+}
+
+template <bool U16, bool REVERSE, bool DICT, bool FIXED_BASE, uint32_t SPLITK = 0>
 __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t* __restrict__ src, uint32_t tbase,
                           uint8_t* ring, uint32_t bar_base, uint32_t lane, ws_device_result* res) {
-  static_assert(DICT || !SPLIT, "only word-dictionary blocks split words");
+  static_assert(DICT || SPLITK == 0, "only word-dictionary blocks split words");
+  constexpr bool SPLIT = SPLITK != 0;
   uint8_t* dst = reinterpret_cast<uint8_t*>(bd.dst);
   const uint32_t n = bd.nbytes;
   const uint32_t W = n / 2;
@@ -476,11 +512,10 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
   const uint32_t groups = (n + WS_GROUP_BYTES - 1) / WS_GROUP_BYTES;
   const bool aligned = (bd.dst & 15u) == 0;
   const uint32_t stream_bytes = (2u * bd.nwords + 15u) & ~15u;
-  SplitRaw split;
+  SplitRaw<SPLIT ? SPLITK : 1u> split;
   uint32_t raw_bytes = 0;
   if (SPLIT) {
-    split.k = ws_split_bits(bd.flags);
-    raw_bytes = ws_split_raw_bytes(W, split.k);
+    raw_bytes = ws_split_raw_bytes(W, SPLITK);
     // The raw section must lie inside the payload; nothing is read or written otherwise.
     if ((uint64_t)stream_bytes + raw_bytes > bd.clen) {
       if (lane == 0) report(res, WS_DEVERR_LENGTH, block);
@@ -561,21 +596,24 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
   };
   // The lane's word pairs r0..r3 of group `grp` applied to the destination
   // vector `old` (escaped words patched in first) and written back.
+  // A split block's raw bits (e0..e3, from raw word rw) fill the zero low bits
+  // of the decoded words, so they join with the same XOR.
   auto finish = [&](uint4* q, uint4 old, uint32_t grp, uint32_t rw, uint32_t r0, uint32_t r1, uint32_t r2,
                     uint32_t r3) {
-    if (SPLIT) split.merge(rw, split.offset(grp), r0, r1, r2, r3);
+    uint32_t e0 = 0, e1 = 0, e2 = 0, e3 = 0;
+    if (SPLIT) split.bits(rw, grp, e0, e1, e2, e3);
     if (DICT && esc.w < (grp + 1) * WS_GROUP_WORDS) esc.patch(grp, lane, r0, r1, r2, r3);
     uint4 v;
     if (U16) {
-      v.x = u16_apply(old.x, r0, REVERSE);
-      v.y = u16_apply(old.y, r1, REVERSE);
-      v.z = u16_apply(old.z, r2, REVERSE);
-      v.w = u16_apply(old.w, r3, REVERSE);
+      v.x = u16_apply(old.x, r0 ^ e0, REVERSE);
+      v.y = u16_apply(old.y, r1 ^ e1, REVERSE);
+      v.z = u16_apply(old.z, r2 ^ e2, REVERSE);
+      v.w = u16_apply(old.w, r3 ^ e3, REVERSE);
     } else {
-      v.x = old.x ^ r0;
-      v.y = old.y ^ r1;
-      v.z = old.z ^ r2;
-      v.w = old.w ^ r3;
+      v.x = old.x ^ r0 ^ e0;
+      v.y = old.y ^ r1 ^ e1;
+      v.z = old.z ^ r2 ^ e2;
+      v.w = old.w ^ r3 ^ e3;
     }
     *q = v;
     ck.add(v.x, v.y, v.z, v.w);
@@ -595,7 +633,9 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
       if (pos >= next_event && !at_event()) break;
       const uint4 old0 = ldg128_early(p);
       const uint4 old1 = ldg128_early(p + WS_GROUP_BYTES / 16);
-      const uint32_t rw0 = SPLIT ? split.load(src, g) : 0u, rw1 = SPLIT ? split.load(src, g + 1) : 0u;
+      // g is even: for K = 1, 2 groups g and g + 1 share a raw word.
+      const uint32_t rw0 = SPLIT ? split.load(src, g) : 0u;
+      const uint32_t rw1 = SPLITK == 4 ? split.load(src, g + 1) : rw0;
       if (lane == 0 && g + 2 + kPrefetchGroups + 2 <= fast_groups)
         prefetch_l2(dst + (g + 2 + kPrefetchGroups) * WS_GROUP_BYTES, 2 * WS_GROUP_BYTES);
       uint32_t rp = ring_s + (pos & (kRingHalfwords - 1)) * 2u;
@@ -670,7 +710,11 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
       }
     }
     uint32_t out[4] = {0, 0, 0, 0};
-    if (SPLIT && g < dec_groups) split.merge(split.load(src, g), split.offset(g), r[0], r[1], r[2], r[3]);
+    if (SPLIT && g < dec_groups) {
+      uint32_t e[4];
+      split.bits(split.load(src, g), g, e[0], e[1], e[2], e[3]);
+      for (int q = 0; q < 4; ++q) r[q] |= e[q];
+    }
     if (DICT && g < dec_groups) esc.patch(g, lane, r[0], r[1], r[2], r[3]);
     apply_chunk_bytes<U16, REVERSE>(dst + off, off, n, r, coded_bytes, bd.tail, out);
     ck.add(out[0], out[1], out[2], out[3]);
@@ -702,12 +746,32 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
   ck.finish(lane, block, res);
 }
 
+// A word-dictionary block, by its split code (0: whole words; else the code
+// the tile's raw-bit table was built for).
+template <bool U16, bool REVERSE, bool FIXED_BASE>
+__device__ __forceinline__ void dict_block(const ws_block_desc& bd, uint32_t block, const uint8_t* __restrict__ src,
+                                           uint32_t tbase, uint8_t* ring, uint32_t bar_base, uint32_t lane,
+                                           ws_device_result* res, uint32_t tile_split) {
+  const uint32_t code = (bd.flags & WS_FLAG_SPLIT_MASK) >> WS_FLAG_SPLIT_SHIFT;
+  if (code == 0) {
+    ans_block<U16, REVERSE, true, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
+  } else if (code != tile_split) {  // the tile's expansion table is for another k
+    if (lane == 0) report(res, WS_DEVERR_KIND, block);
+  } else if (code == 1) {
+    ans_block<U16, REVERSE, true, FIXED_BASE, 1>(bd, block, src, tbase, ring, bar_base, lane, res);
+  } else if (code == 2) {
+    ans_block<U16, REVERSE, true, FIXED_BASE, 2>(bd, block, src, tbase, ring, bar_base, lane, res);
+  } else {
+    ans_block<U16, REVERSE, true, FIXED_BASE, 4>(bd, block, src, tbase, ring, bar_base, lane, res);
+  }
+}
+
 // One block by its kind. FIXED_BASE: the table region starts at the shared
 // address kFixedTableBase, which the lookups then take as an immediate offset.
 template <bool REVERSE, bool FIXED_BASE>
 __device__ __forceinline__ void run_block(const ws_block_desc& bd, uint32_t block, const uint8_t* __restrict__ src,
                                           uint32_t tbase, uint8_t* ring, uint32_t bar_base, uint32_t lane,
-                                          ws_device_result* res) {
+                                          ws_device_result* res, uint32_t tile_split) {
   switch (bd.kind) {
     case WS_KIND_RAW:
       raw_block(bd, block, src, lane, res);
@@ -723,16 +787,10 @@ __device__ __forceinline__ void run_block(const ws_block_desc& bd, uint32_t bloc
       }
       break;
     case WS_KIND_DICT_XOR:
-      if (bd.flags & WS_FLAG_SPLIT_MASK)
-        ans_block<false, REVERSE, true, FIXED_BASE, true>(bd, block, src, tbase, ring, bar_base, lane, res);
-      else
-        ans_block<false, REVERSE, true, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
+      dict_block<false, REVERSE, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res, tile_split);
       break;
     case WS_KIND_DICT_U16:
-      if (bd.flags & WS_FLAG_SPLIT_MASK)
-        ans_block<true, REVERSE, true, FIXED_BASE, true>(bd, block, src, tbase, ring, bar_base, lane, res);
-      else
-        ans_block<true, REVERSE, true, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
+      dict_block<true, REVERSE, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res, tile_split);
       break;
     default:
       if (lane == 0) report(res, WS_DEVERR_KIND, block);
@@ -773,7 +831,7 @@ __device__ __forceinline__ void apply_tile(const ws_tile_desc& tile, const ws_bl
   if (CHECKED) {
     // Uniform over the CTA: either every thread returns here or none does.
     const bool tile_ok = tile.nblocks <= kWarps && (uint64_t)tile.first_block + tile.nblocks <= lim.nblocks &&
-                         (tile.table == WS_NO_TABLE || tile.table < lim.ntables);
+                         (tile.table == WS_NO_TABLE || tile.table < lim.ntables) && tile.split <= 3;
     if (!tile_ok) {
       if (threadIdx.x == 0) report(res, WS_DEVERR_BOUNDS, tile.first_block);
       return;
@@ -789,6 +847,7 @@ __device__ __forceinline__ void apply_tile(const ws_tile_desc& tile, const ws_bl
 #pragma unroll
     for (uint32_t k = 0; k < 8; ++k) row[(k + t) & 7u] = v;
   }
+  if (tile.split != 0 && threadIdx.x < 256) build_split_table(ws_split_bits(tile.split << WS_FLAG_SPLIT_SHIFT), threadIdx.x);
   const uint32_t bar_base = smem_addr(smem + kBarOffset) + warp * 16u;
   if (lane == 0) {
     mbar_init(bar_base, 1);
@@ -807,9 +866,9 @@ __device__ __forceinline__ void apply_tile(const ws_tile_desc& tile, const ws_bl
   uint8_t* ring = smem + kRingOffset + warp * kRingStride;
   const uint32_t tbase = smem_addr(tbl);
   if (tbase == kFixedTableBase)
-    run_block<REVERSE, true>(bd, block, src, tbase, ring, bar_base, lane, res);
+    run_block<REVERSE, true>(bd, block, src, tbase, ring, bar_base, lane, res, tile.split);
   else
-    run_block<REVERSE, false>(bd, block, src, tbase, ring, bar_base, lane, res);
+    run_block<REVERSE, false>(bd, block, src, tbase, ring, bar_base, lane, res, tile.split);
 }
 
 template <bool REVERSE>

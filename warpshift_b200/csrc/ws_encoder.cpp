@@ -379,6 +379,9 @@ double dict_tables(const std::vector<uint16_t>& words, const uint64_t* sym_count
 
 namespace {
 
+// Estimated size a split-word dictionary must save over the whole-word one.
+constexpr double kSplitGainPct = 3.0;
+
 // The best dictionary of one symbol alphabet (distinct values `words`,
 // increasing, with `counts`): every value a symbol, or (escapes) the K most
 // frequent ones (ties: smaller value first) plus the escape symbol. Returns the
@@ -493,7 +496,12 @@ void choose_coding(const uint64_t counts[2][256], const std::vector<uint16_t>& w
       const double raw_bytes = (double)coded_blocks * ws_split_raw_bytes(WS_BLOCK_BYTES / 2, k);
       size_t kept;
       const double est = best_dictionary(sw, sc, raw_bytes, coded_blocks, co, &kept, nullptr);
-      if (best_k < 0 || est < best) {
+      // A split block decodes more slowly (its raw bits are a second read and
+      // a table lookup per group), so unless forced a split coding must beat
+      // the whole-word dictionary by kSplitGainPct of its size.
+      const double bar = (best_k == 0 && co.split == 0) ? best * (1.0 - kSplitGainPct / 100.0) : best;
+      const bool wins = best_k < 0 || est < bar;
+      if (wins) {
         best = est;
         best_k = (int)k;
         best_kept = kept;
@@ -525,7 +533,7 @@ void append_split_raw(const uint16_t* v, uint32_t W, uint32_t k, std::vector<uin
   const uint32_t per = 4u / k, mask = (1u << k) - 1u;
   for (uint32_t w = 0; w < W; ++w) {
     const uint32_t g = w / WS_GROUP_WORDS, lane = (w % WS_GROUP_WORDS) / WS_WORDS_PER_LANE, j = w % WS_WORDS_PER_LANE;
-    const uint32_t bit = ((j & 1u) ? 16u : 0u) + (g % per) * 4u * k + (j >> 1) * k;
+    const uint32_t bit = (g % per) * 8u * k + j * k;
     raw[(g / per) * WS_LANES + lane] |= ((uint32_t)v[w] & mask) << bit;
   }
   const size_t at = payload->size();

@@ -75,13 +75,13 @@ enum ws_kind {
 // word with the low k bits zero, so decoding is unchanged). The raw section
 // follows the stream at byte align16(2 * nwords) and precedes any escape list;
 // it is read, not staged. It holds uint32 raw words: G = 4 / k groups share one
-// word per lane, raw word (g / G) * 32 + lane for group g; inside it group g
-// starts at bit o = (g % G) * 4k, and the lane's word pair j (words 2j, 2j+1 of
-// its 8) keeps word 2j's bits at [o + jk, o + jk + k) and word 2j+1's at
-// [16 + o + jk, 16 + o + jk + k), so one shift and one mask put a pair's bits
-// in place. Words past the block's end have zero bits. The section is
-// 4 * 32 * ceil(ceil(W / 256) / G) bytes (a multiple of 16). An escaped word's
-// list entry carries the word with its low k bits cleared.
+// word per lane, raw word (g / G) * 32 + lane for group g. Inside it the lane's
+// 8k bits of group g are bytes (g % G) * k .. (g % G) * k + k - 1, and its word
+// j (of the 8 it owns in the group) has bits [8k * (g % G) + jk, ... + k): a
+// byte holds the bits of 8 / k consecutive words, so the kernel expands one
+// byte through a 256-entry table. Words past the block's end have zero bits.
+// The section is 4 * 32 * ceil(ceil(W / 256) / G) bytes (a multiple of 16). An
+// escaped word's list entry carries the word with its low k bits cleared.
 #define WS_FLAG_SPLIT_SHIFT 2u
 #define WS_FLAG_SPLIT_MASK 0x0Cu
 
@@ -109,7 +109,7 @@ typedef struct ws_tile_desc {
   uint32_t first_block;
   uint32_t nblocks;
   uint32_t table;  // packet table index (512 entries each), or WS_NO_TABLE
-  uint32_t pad;
+  uint32_t split;  // the packet's split code (flags bits 2-3 of its split-word blocks, shifted down), or 0
 } ws_tile_desc;
 #define WS_NO_TABLE 0xFFFFFFFFu
 

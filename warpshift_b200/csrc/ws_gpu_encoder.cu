@@ -438,7 +438,7 @@ __global__ void compact_kernel(const CompactJob* __restrict__ jobs, const BlockJ
         load_words(blk, g * WS_GROUP_WORDS + lane * WS_WORDS_PER_LANE, W, aligned, job.u16 != 0, v);
 #pragma unroll
         for (uint32_t j = 0; j < 8; ++j)
-          acc |= ((uint32_t)v[j] & mask) << (((j & 1u) ? 16u : 0u) + gg * 4u * k + (j >> 1) * k);
+          acc |= ((uint32_t)v[j] & mask) << (gg * 8u * k + j * k);
       }
       raw[r] = acc;
     }

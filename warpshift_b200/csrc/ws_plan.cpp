@@ -315,7 +315,11 @@ int layout(ws_plan* p, const ws_tensor_desc* tensors, const std::vector<PacketRe
         t.first_block = (uint32_t)p->blocks.size();
         t.nblocks = (uint32_t)std::min<size_t>(WS_TILE_BLOCKS, e.blocks.size() - k);
         t.table = table;
-        t.pad = 0;
+        // Every split-word block of a packet has the packet's split code; the
+        // kernel expands that code's raw-bit table once per tile.
+        t.split = 0;
+        for (size_t q = k; q < k + t.nblocks; ++q)
+          t.split = std::max<uint32_t>(t.split, (e.blocks[q].flags & WS_FLAG_SPLIT_MASK) >> WS_FLAG_SPLIT_SHIFT);
         p->tiles.push_back(t);
       }
       ws_block_desc d;
