@@ -75,7 +75,8 @@ typedef struct ws_build_options {
                                WS_ERR_NOMEM */
   int32_t split;            /* split-word dictionaries (the low k = 1, 2 or 4 bits of every word
                                stored raw, the rest coded): 0 (default) the k estimated smallest,
-                               k = 0 included; < 0 never; 1, 2 or 4: that k whenever eligible */
+                               a split one only when 3 % smaller than whole words (split blocks
+                               decode more slowly); < 0 never; 1, 2 or 4: that k whenever eligible */
 } ws_build_options;
 
 typedef struct ws_plan_stats {

@@ -89,8 +89,9 @@ class DeltaWeights:
     the GPU), ``encode_batch_bytes`` (GPU encoder batch; 0 = 512 MiB),
     ``escapes`` (dictionaries with escape lists: 0 when smaller, -1 never, 1
     whenever eligible), ``split`` (split-word dictionaries, whose words' low k
-    bits are stored raw: 0 the k estimated smallest, -1 never, 1 / 2 / 4 that k
-    whenever eligible) and ``host_fallback`` (when the GPU encoder cannot get
+    bits are stored raw: 0 the k estimated smallest, a split one only when 3 %
+    smaller than whole words, -1 never, 1 / 2 / 4 that k whenever eligible)
+    and ``host_fallback`` (when the GPU encoder cannot get
     its device buffers, encode on host threads instead of raising
     RuntimeError; off by default). ``save`` / ``load`` persist a package
     across restarts.
