@@ -210,13 +210,18 @@ def generate_on_device(spec, device, scale):
     return cpu_base, gpu
 
 
-def measure_h2d(device, group=None) -> float:
-    """Pinned host->device GB/s of this rank, all ranks copying at the same time
-    (they share the host's links, as in the end-to-end switch)."""
+def measure_h2d(device, nbytes: int, group=None) -> tuple[float, float]:
+    """The host->device half of a switch alone: this rank copies `nbytes` (its
+    stream's size) from pinned host memory, in 1 GiB pieces, with every rank
+    starting together as in the end-to-end switch, so ranks that share host
+    links share them here too and a rank whose peers finish early speeds up as
+    it does in the switch. Returns (GB/s, ms) of this rank's copies."""
     import torch
     import torch.distributed as dist
 
-    n = 1 << 30
+    if nbytes <= 0:
+        return float("nan"), 0.0
+    n = min(1 << 30, nbytes)
     src = torch.empty(n, dtype=torch.uint8, pin_memory=True)
     dst = torch.empty(n, dtype=torch.uint8, device=device)
     dst.copy_(src, non_blocking=True)
@@ -225,13 +230,14 @@ def measure_h2d(device, group=None) -> float:
         dist.barrier(group=group)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
-    for _ in range(3):
-        dst.copy_(src, non_blocking=True)
+    for off in range(0, nbytes, n):
+        k = min(n, nbytes - off)
+        dst[:k].copy_(src[:k], non_blocking=True)
     e.record()
     torch.cuda.synchronize(device)
-    gbs = 3 * n / (s.elapsed_time(e) * 1e-3) / 1e9
+    ms = s.elapsed_time(e)
     del src, dst
-    return gbs
+    return nbytes / (ms * 1e-3) / 1e9, ms
 
 
 def reference_workload(spec, scale: float, policy: str, budget_bytes: int, threads: int):
@@ -584,7 +590,7 @@ def run_ours(args) -> None:
     C = int(native.arena_bytes)
     touched = int(native.touched_bytes)
     meta = int(native.metadata_bytes)
-    h2d_gbs = measure_h2d(device, group) if not args.skip_e2e else float("nan")
+    h2d_gbs, h2d_ms = measure_h2d(device, C, group) if not args.skip_e2e else (float("nan"), 0.0)
     stream = delta.compute_stream
 
     def barrier():
@@ -730,9 +736,10 @@ def run_ours(args) -> None:
         entry = json.loads(traffic_file.read_text()).get(f"{args.workload}/{args.policy}/{args.scale}")
         if entry:
             traffic = entry["dram_bytes_per_launch"]
-    # Each rank's end-to-end bound uses its own concurrently measured link rate;
-    # the switch time is the max over ranks, so is the bound.
-    rank_roof_ms = max(C / (h2d_gbs * 1e9) if h2d_gbs == h2d_gbs else 0.0, algo_bytes / (pk["hbm_gbs"] * 1e9)) * 1e3
+    # Each rank's end-to-end bound is the time its own stream's copy took with
+    # every rank copying at once (or its kernel's HBM bound, when longer); the
+    # switch ends with its slowest rank, so the group's bound is their maximum.
+    rank_roof_ms = max(h2d_ms, algo_bytes / (pk["hbm_gbs"] * 1e9) * 1e3)
     rank_e2e_ms = e2e_ms / args.steps if e2e_ms is not None else None
     t_roof_ms = max_over_ranks(rank_roof_ms)
     # Per-rank fraction of its own roofline; the minimum over ranks is reported.
@@ -794,7 +801,8 @@ def run_ours(args) -> None:
             "h2d_bytes_per_step": C,
             "d2h_bytes_per_step": 16,
             "h2d_gbs_measured": round(h2d_slowest, 2),
-            "h2d_measurement": "pinned 1 GiB copies, all ranks at once; slowest rank",
+            "h2d_measurement": "each rank copies its stream's size from pinned memory (1 GiB pieces), all ranks "
+                               "starting together; slowest rank's rate",
             "roofline_ms": round(t_roof_ms, 3),
             "roofline_frac": round(t_roof_ms / (e2e_ms_max / args.steps), 3),
             "min_rank_roofline_frac": round(min_rank_frac, 3) if min_rank_frac else None,
