@@ -748,27 +748,35 @@ __device__ void ans_block(const ws_block_desc& bd, uint32_t block, const uint8_t
 
 // A word-dictionary block, by its split code (0: whole words; else the code
 // the tile's raw-bit table was built for).
-template <bool U16, bool REVERSE, bool FIXED_BASE>
+// Which tiles a kernel instantiation decodes: tiles without split-word blocks
+// (kWholeTiles), tiles of a packet that splits words (kSplitTiles), or both
+// (kAnyTiles, the allocation-free entry point, whose tiles the host cannot
+// see). Keeping the split decoders out of the whole-word kernel keeps its
+// register allocation free of their spills.
+enum TileMode : int { kWholeTiles = 0, kSplitTiles = 1, kAnyTiles = 2 };
+
+template <bool U16, bool REVERSE, bool FIXED_BASE, int MODE>
 __device__ __forceinline__ void dict_block(const ws_block_desc& bd, uint32_t block, const uint8_t* __restrict__ src,
                                            uint32_t tbase, uint8_t* ring, uint32_t bar_base, uint32_t lane,
                                            ws_device_result* res, uint32_t tile_split) {
   const uint32_t code = (bd.flags & WS_FLAG_SPLIT_MASK) >> WS_FLAG_SPLIT_SHIFT;
-  if (code == 0) {
-    ans_block<U16, REVERSE, true, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
-  } else if (code != tile_split) {  // the tile's expansion table is for another k
+  if (code != tile_split) {  // the tile's expansion table is for another k (or none)
     if (lane == 0) report(res, WS_DEVERR_KIND, block);
-  } else if (code == 1) {
-    ans_block<U16, REVERSE, true, FIXED_BASE, 1>(bd, block, src, tbase, ring, bar_base, lane, res);
-  } else if (code == 2) {
-    ans_block<U16, REVERSE, true, FIXED_BASE, 2>(bd, block, src, tbase, ring, bar_base, lane, res);
-  } else {
-    ans_block<U16, REVERSE, true, FIXED_BASE, 4>(bd, block, src, tbase, ring, bar_base, lane, res);
+  } else if (code == 0) {
+    if constexpr (MODE != kSplitTiles) ans_block<U16, REVERSE, true, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
+  } else if constexpr (MODE != kWholeTiles) {
+    if (code == 1)
+      ans_block<U16, REVERSE, true, FIXED_BASE, 1>(bd, block, src, tbase, ring, bar_base, lane, res);
+    else if (code == 2)
+      ans_block<U16, REVERSE, true, FIXED_BASE, 2>(bd, block, src, tbase, ring, bar_base, lane, res);
+    else
+      ans_block<U16, REVERSE, true, FIXED_BASE, 4>(bd, block, src, tbase, ring, bar_base, lane, res);
   }
 }
 
 // One block by its kind. FIXED_BASE: the table region starts at the shared
 // address kFixedTableBase, which the lookups then take as an immediate offset.
-template <bool REVERSE, bool FIXED_BASE>
+template <bool REVERSE, bool FIXED_BASE, int MODE>
 __device__ __forceinline__ void run_block(const ws_block_desc& bd, uint32_t block, const uint8_t* __restrict__ src,
                                           uint32_t tbase, uint8_t* ring, uint32_t bar_base, uint32_t lane,
                                           ws_device_result* res, uint32_t tile_split) {
@@ -778,19 +786,21 @@ __device__ __forceinline__ void run_block(const ws_block_desc& bd, uint32_t bloc
       break;
     case WS_KIND_ANS_XOR:
     case WS_KIND_ANS_U16:
-      if (bd.flags & WS_FLAG_SPLIT_MASK) {  // byte planes never split words
+      // Byte planes never split words, and a packet that splits words has none.
+      if ((bd.flags & WS_FLAG_SPLIT_MASK) || tile_split != 0) {
         if (lane == 0) report(res, WS_DEVERR_KIND, block);
-      } else if (bd.kind == WS_KIND_ANS_XOR) {
-        ans_block<false, REVERSE, false, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
-      } else {
-        ans_block<true, REVERSE, false, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
+      } else if constexpr (MODE != kSplitTiles) {
+        if (bd.kind == WS_KIND_ANS_XOR)
+          ans_block<false, REVERSE, false, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
+        else
+          ans_block<true, REVERSE, false, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res);
       }
       break;
     case WS_KIND_DICT_XOR:
-      dict_block<false, REVERSE, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res, tile_split);
+      dict_block<false, REVERSE, FIXED_BASE, MODE>(bd, block, src, tbase, ring, bar_base, lane, res, tile_split);
       break;
     case WS_KIND_DICT_U16:
-      dict_block<true, REVERSE, FIXED_BASE>(bd, block, src, tbase, ring, bar_base, lane, res, tile_split);
+      dict_block<true, REVERSE, FIXED_BASE, MODE>(bd, block, src, tbase, ring, bar_base, lane, res, tile_split);
       break;
     default:
       if (lane == 0) report(res, WS_DEVERR_KIND, block);
@@ -821,11 +831,17 @@ __device__ __forceinline__ bool block_in_bounds(const ws_block_desc& bd, uint64_
 // `payload_offset`. With CHECKED, every descriptor is first checked against
 // `lim`; one that points outside the caller's arrays is reported as
 // WS_DEVERR_BOUNDS and not followed.
-template <bool REVERSE, bool CHECKED>
+template <bool REVERSE, bool CHECKED, int MODE>
 __device__ __forceinline__ void apply_tile(const ws_tile_desc& tile, const ws_block_desc* __restrict__ blocks,
                                            const uint32_t* __restrict__ tables, const uint8_t* __restrict__ payload,
                                            uint64_t payload_offset, ws_device_result* res, DescLimits lim) {
   extern __shared__ __align__(1024) uint8_t smem[];
+  // The host picks the instantiation from the tiles' kinds; a tile of the other
+  // kind is reported, not decoded.
+  if (MODE != kAnyTiles && (tile.split != 0) != (MODE == kSplitTiles)) {
+    if (threadIdx.x == 0) report(res, WS_DEVERR_KIND, tile.first_block);
+    return;
+  }
   uint32_t* tbl = reinterpret_cast<uint32_t*>(smem);
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   if (CHECKED) {
@@ -866,44 +882,60 @@ __device__ __forceinline__ void apply_tile(const ws_tile_desc& tile, const ws_bl
   uint8_t* ring = smem + kRingOffset + warp * kRingStride;
   const uint32_t tbase = smem_addr(tbl);
   if (tbase == kFixedTableBase)
-    run_block<REVERSE, true>(bd, block, src, tbase, ring, bar_base, lane, res, tile.split);
+    run_block<REVERSE, true, MODE>(bd, block, src, tbase, ring, bar_base, lane, res, tile.split);
   else
-    run_block<REVERSE, false>(bd, block, src, tbase, ring, bar_base, lane, res, tile.split);
+    run_block<REVERSE, false, MODE>(bd, block, src, tbase, ring, bar_base, lane, res, tile.split);
 }
 
-template <bool REVERSE>
+template <bool REVERSE, int MODE>
 __global__ void __launch_bounds__(kThreads, 2)
     ws_apply_kernel(const ws_tile_desc* __restrict__ tiles, uint32_t tile_begin,
                     const ws_block_desc* __restrict__ blocks, const uint32_t* __restrict__ tables,
                     const uint8_t* __restrict__ payload, uint64_t payload_offset, ws_device_result* res) {
-  apply_tile<REVERSE, false>(tiles[tile_begin + blockIdx.x], blocks, tables, payload, payload_offset, res,
-                             DescLimits{});
+  apply_tile<REVERSE, false, MODE>(tiles[tile_begin + blockIdx.x], blocks, tables, payload, payload_offset, res,
+                                   DescLimits{});
 }
 
 }  // namespace
 
 size_t apply_smem_bytes() { return kSmemBytes; }
 
+using ApplyKernel = void (*)(const ws_tile_desc*, uint32_t, const ws_block_desc*, const uint32_t*, const uint8_t*,
+                             uint64_t, ws_device_result*);
+
+// The instantiation for a launch range holding the given tile kinds: whole-word
+// tiles only, split-word tiles only, or both (one kernel that decodes either).
+ApplyKernel apply_kernel(int reverse, uint32_t kinds) {
+  if (kinds == kTilesWhole) return reverse ? ws_apply_kernel<true, kWholeTiles> : ws_apply_kernel<false, kWholeTiles>;
+  if (kinds == kTilesSplit) return reverse ? ws_apply_kernel<true, kSplitTiles> : ws_apply_kernel<false, kSplitTiles>;
+  return reverse ? ws_apply_kernel<true, kAnyTiles> : ws_apply_kernel<false, kAnyTiles>;
+}
+
 cudaError_t prime_kernels() {
-  // Loads both kernel instantiations (lazy module loading) and sets their
+  // Loads every kernel instantiation (lazy module loading) and sets its
   // shared-memory limit, so the first apply of each direction pays nothing.
-  cudaError_t e = cudaFuncSetAttribute(ws_apply_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(ws_apply_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+  cudaError_t e = cudaSuccess;
+  for (int reverse = 0; reverse < 2 && e == cudaSuccess; ++reverse)
+    for (uint32_t kinds = 1; kinds <= 3 && e == cudaSuccess; ++kinds)
+      e = cudaFuncSetAttribute(apply_kernel(reverse, kinds), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)kSmemBytes);
   return e;
 }
 
 cudaError_t launch_apply(const ws_tile_desc* tiles, uint32_t tile_begin, uint32_t ntiles,
                          const ws_block_desc* blocks, const uint32_t* tables, const uint8_t* payload,
-                         uint64_t payload_offset, ws_device_result* result, int reverse, cudaStream_t stream) {
+                         uint64_t payload_offset, ws_device_result* result, int reverse, uint32_t kinds,
+                         cudaStream_t stream, uint32_t* launched) {
   if (ntiles == 0) return cudaSuccess;
-  auto kernel = reverse ? ws_apply_kernel<true> : ws_apply_kernel<false>;
+  const ApplyKernel kernel = apply_kernel(reverse, kinds);
   // Set on every launch: the attribute is per device context and costs ~1 us.
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
   if (e != cudaSuccess) return e;
   kernel<<<ntiles, kThreads, kSmemBytes, stream>>>(tiles, tile_begin, blocks, tables, payload, payload_offset,
                                                      result);
-  return cudaGetLastError();
+  e = cudaGetLastError();
+  if (e == cudaSuccess && launched) ++*launched;
+  return e;
 }
 
 }  // namespace ws
@@ -936,7 +968,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     ws_apply_noalloc_kernel(const ws_tile_desc* __restrict__ tiles, const ws_block_desc* __restrict__ blocks,
                             const uint32_t* __restrict__ tables, const uint8_t* __restrict__ payload,
                             DescLimits lim, ws_device_result* scratch) {
-  apply_tile<REVERSE, true>(tiles[blockIdx.x], blocks, tables, payload, 0, scratch + blockIdx.x, lim);
+  apply_tile<REVERSE, true, kAnyTiles>(tiles[blockIdx.x], blocks, tables, payload, 0, scratch + blockIdx.x, lim);
 }
 
 // Sums the per-tile slots [0, n) into slot WS_NOALLOC_MAX_TILES (one CTA).

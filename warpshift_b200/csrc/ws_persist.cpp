@@ -171,9 +171,9 @@ std::string check_descriptors(const ws_plan* p) {
     if (td.table == WS_NO_TABLE ? coded : td.table >= ntables) return "tile " + std::to_string(i) + " has a bad table";
     const bool split_ok =
         td.split <= 3 && std::all_of(p->blocks.begin() + td.first_block, p->blocks.begin() + td.first_block + td.nblocks,
-                                     [&](const ws_block_desc& d) {
+                                     [&](const ws_block_desc& d) {  // coded blocks share the tile's code
                                        const uint32_t c = (d.flags & WS_FLAG_SPLIT_MASK) >> WS_FLAG_SPLIT_SHIFT;
-                                       return c == 0 || c == td.split;
+                                       return d.kind == WS_KIND_RAW ? c == 0 : c == td.split;
                                      });
     if (!split_ok) return "tile " + std::to_string(i) + " has blocks of another split code";
   }

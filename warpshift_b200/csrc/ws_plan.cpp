@@ -395,7 +395,7 @@ int form_batches(ws_plan* p, std::string* err) {
   const uint64_t cap =
       std::min<uint64_t>(p->opts.batch_bytes, std::max<uint64_t>(16ull << 20, p->arena_bytes / 64));
   uint64_t limit = std::max<uint64_t>(cap / 16, 1ull << 20);
-  Batch cur{0, 0, 0, 0, 0};
+  Batch cur{0, 0, 0, 0, 0, 0};
   bool open = false;
   uint32_t chunk = 0;
   for (uint32_t t = 0; t < p->tiles.size(); ++t) {
@@ -414,11 +414,12 @@ int form_batches(ws_plan* p, std::string* err) {
       limit = std::min(limit * 4, cap);
     }
     if (!open) {
-      cur = Batch{t, t, first.src, 0, chunk};
+      cur = Batch{t, t, first.src, 0, chunk, 0};
       open = true;
     }
     cur.tile_end = t + 1;
     cur.bytes += bytes;
+    cur.kinds |= td.split ? ws::kTilesSplit : ws::kTilesWhole;
   }
   if (open) p->batches.push_back(cur);
   p->stats.batches = p->batches.size();
@@ -634,9 +635,10 @@ static int ws_apply_async_impl(ws_plan* p, int reverse, void* compute_stream, vo
   WS_CUDA_TRY(cudaMemsetAsync(p->d_result, 0, sizeof(ws_device_result), comp));
   if (p->d_resident || p->arena_bytes == 0) {
     if (!p->tiles.empty()) {
+      uint32_t kinds = 0;
+      for (const Batch& bt : p->batches) kinds |= bt.kinds;
       WS_CUDA_TRY(ws::launch_apply(p->d_tiles, 0, (uint32_t)p->tiles.size(), p->d_blocks, p->d_tables,
-                                   p->d_resident, 0, p->d_result, reverse, comp));
-      launches = 1;
+                                   p->d_resident, 0, p->d_result, reverse, kinds, comp, &launches));
     }
   } else {
     // Staged: batch b is copied into slot b % nslots on the copy stream and
@@ -658,10 +660,9 @@ static int ws_apply_async_impl(ws_plan* p, int reverse, void* compute_stream, vo
       WS_CUDA_TRY(cudaEventRecord(p->copy_done[slot], copy));
       WS_CUDA_TRY(cudaStreamWaitEvent(run, p->copy_done[slot], 0));
       WS_CUDA_TRY(ws::launch_apply(p->d_tiles, bt.tile_begin, bt.tile_end - bt.tile_begin, p->d_blocks, p->d_tables,
-                                   p->d_slots[slot], bt.arena_off, p->d_result, reverse, run));
+                                   p->d_slots[slot], bt.arena_off, p->d_result, reverse, bt.kinds, run, &launches));
       WS_CUDA_TRY(cudaEventRecord(p->compute_done[slot], run));
       h2d += bt.bytes;
-      ++launches;
     }
     WS_CUDA_TRY(cudaEventRecord(p->aux_done, p->aux_stream));
     WS_CUDA_TRY(cudaStreamWaitEvent(comp, p->aux_done, 0));

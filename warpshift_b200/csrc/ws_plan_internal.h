@@ -17,6 +17,7 @@ struct Batch {
   uint32_t tile_begin, tile_end;
   uint64_t arena_off, bytes;
   uint32_t chunk;  // arena chunk holding the whole batch
+  uint32_t kinds;  // kTilesWhole | kTilesSplit: the tile kinds in the batch (one kernel launch each)
 };
 
 }  // namespace ws
